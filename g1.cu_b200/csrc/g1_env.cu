@@ -1,0 +1,865 @@
+// g1_env.cu -- the B200 fused G1 rollout and its C-ABI (libg1env.so).
+//
+// Drop-in for the reference's build/libg1env.so (Infatoshi/g1.cu src/g1_env.cu:361-476):
+// same exported names, argument types, buffer layouts and ownership, so the reference's
+// ctypes trainer (scripts/ppo.py, scripts/ppo_fused.py) loads this library unchanged.
+//
+// Execution model (sm_100a):
+//   * one persistent kernel per call; a CTA owns a contiguous block of worlds for the whole
+//     horizon (a CTA per SM: the grid is sized to the SM count);
+//   * per control step the CTA first runs the POLICY phase over its whole world block --
+//     observations, normalisation, the actor-critic MLP as a dense contraction staged in
+//     shared memory, Philox Gaussian sampling, trajectory writes -- then the PHYSICS phase,
+//     where each warp takes one world at a time from the block (shared-memory queue) and
+//     advances it S substeps with its frame in shared memory (g1_physics.cuh);
+//   * world state (qpos, qvel, previous action, episode step) stays in HBM/L2 between
+//     control steps ([N,36], [N,35], [N,29], [N] like the reference's EnvState).
+// Errors: C-ABI functions keep the reference's void returns; failures are recorded and
+// read with g1_env_last_error() instead of exit(1) (the reference's CK, g1_env.cu:33-34).
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+
+#include "g1_physics.cuh"
+#include "../../include/g1env.h"
+
+using namespace g1;
+
+#define OBS_DIM 100
+#define ACT_DIM 29
+#define CMD_VX 0.8f
+#define X_FIN 5.0f
+#define FINISH_BONUS 50.0f
+#define ACT_SCALE 0.5f
+
+#define NWARPS 14
+#define NTHREADS (NWARPS * 32)
+#define MAX_WB 64          // worlds per CTA block, upper bound (MLP activations in smem)
+#define MAX_HIDDEN 4
+#define XSTR 104           // normalized-obs row stride (floats)
+
+__constant__ G1Tables c_tab;
+
+// ------------------------------------------------------------------ error state
+static std::mutex g_err_mu;
+static std::string g_last_error;
+static int g_last_code = 0;
+static void set_error(int code, const char* where, const char* what) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    g_last_code = code;
+    char buf[512];
+    snprintf(buf, sizeof buf, "%s: %s", where, what);
+    g_last_error = buf;
+}
+#define CKR(call, ret)                                                       \
+    do {                                                                     \
+        cudaError_t e_ = (call);                                             \
+        if (e_ != cudaSuccess) {                                             \
+            set_error((int)e_, __func__, cudaGetErrorString(e_));            \
+            return ret;                                                      \
+        }                                                                    \
+    } while (0)
+
+// ------------------------------------------------------------------ Philox4x32-10
+// Salmon et al., SC'11.  Counter = {world id, tick lo, tick hi, purpose<<16 | index},
+// key = seed (lo, hi).  Identical layout in the CPU oracle.
+__device__ __forceinline__ uint4 philox(uint4 c, uint2 k) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        if (r) { k.x += 0x9E3779B9u; k.y += 0xBB67AE85u; }
+        uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
+        uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
+        c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    }
+    return c;
+}
+enum : uint32_t { RNG_ACTION = 1, RNG_AUTORESET = 2, RNG_RESET = 3 };
+__device__ __forceinline__ uint4 rng_draw(uint64_t seed, uint32_t world, uint64_t tick, uint32_t purpose, uint32_t idx) {
+    return philox(make_uint4(world, (uint32_t)tick, (uint32_t)(tick >> 32), (purpose << 16) | idx),
+                  make_uint2((uint32_t)seed, (uint32_t)(seed >> 32)));
+}
+__device__ __forceinline__ float u01_open(uint32_t x) { return (float)((x >> 8) + 1u) * (1.0f / 16777216.0f); }
+__device__ __forceinline__ float u01(uint32_t x) { return (float)(x >> 8) * (1.0f / 16777216.0f); }
+
+// ------------------------------------------------------------------ kernel parameters
+enum Mode : int { MODE_ROLLOUT = 0, MODE_STEP = 1, MODE_PHYS = 2 };
+
+struct Params {
+    int N, S, pgs, H, K, mode, wb;
+    float mu;
+    float *qp, *qv, *pa;
+    int* steps;
+    uint64_t seed;
+    uint32_t world0;
+    uint64_t tick0;
+    // policy (repacked: per layer W^T [nin][nout] then bias; head W^T [nlast][32], bias[32], log_std[32])
+    const float* WT;
+    int nh, hid[MAX_HIDDEN], act;
+    const float *mean, *var;
+    float *O, *A, *LP, *V, *R, *D, *Vlast;
+    // host-loop step
+    const float* act_in;
+    float *obs_out, *rew_out, *done_out;
+    int* ncon_hist;  // [MAXCON+1] contact-count histogram (substeps), may be null
+    int lockstep;    // warps of a CTA walk their worlds in lockstep (named barrier per substep)
+};
+
+// ------------------------------------------------------------------ observations
+// compute_obs (g1_env.cu:46-53, 69-81) for one world by one warp; returns element i.
+__device__ __forceinline__ float obs_elem(int i, const float* qp, const float* qv, const float* pa, const G1Tables& T) {
+    if (i < 6) return qv[i];
+    if (i < 9) {
+        float m[9];
+        qmat(ld4(qp + 3), m);
+        return -m[i];  // -third row of R_base
+    }
+    if (i < 38) return qp[T.act_qadr[i - 9]];
+    if (i < 67) return qv[T.act_dof[i - 38]];
+    if (i < 96) return pa[i - 67];
+    return i == 96 ? CMD_VX : 0.f;
+}
+
+// ------------------------------------------------------------------ policy phase
+// out[w][o] = act(b[o] + sum_i W[o][i] in[w][i]), i ascending (mlp_forward order,
+// g1_env.cu:230-237).  WT is [nin][nout] (coalesced across output lanes); a thread owns 2
+// outputs x 4 worlds so each weight pair is loaded once per 4 worlds.
+__device__ __noinline__ void cta_dense(const float* __restrict__ WT, int wstr, const float* __restrict__ bias, int nin, int nout,
+                          const float* in, int istr, float* out, int ostr, int nw, int act) {
+    const int nog = (nout + 1) >> 1, nwg = (nw + 3) >> 2;
+    for (int it = threadIdx.x; it < nog * nwg; it += blockDim.x) {
+        const int og = it % nog, wg = it / nog;
+        const int o0 = 2 * og, w0 = 4 * wg;
+        const bool has1 = o0 + 1 < nout;
+        float acc[4][2];
+        const float b0 = bias[o0], b1 = has1 ? bias[o0 + 1] : 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { acc[k][0] = b0; acc[k][1] = b1; }
+        const float* xr[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xr[k] = in + (size_t)min(w0 + k, nw - 1) * istr;
+        for (int i = 0; i < nin; i += 4) {
+            float2 wv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                wv[q] = (i + q < nin) ? (has1 ? __ldg(reinterpret_cast<const float2*>(WT + (size_t)(i + q) * wstr + o0))
+                                              : make_float2(__ldg(WT + (size_t)(i + q) * wstr + o0), 0.f))
+                                      : make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float4 x = *reinterpret_cast<const float4*>(xr[k] + i);
+                acc[k][0] += wv[0].x * x.x; acc[k][1] += wv[0].y * x.x;
+                if (i + 1 < nin) { acc[k][0] += wv[1].x * x.y; acc[k][1] += wv[1].y * x.y; }
+                if (i + 2 < nin) { acc[k][0] += wv[2].x * x.z; acc[k][1] += wv[2].y * x.z; }
+                if (i + 3 < nin) { acc[k][0] += wv[3].x * x.w; acc[k][1] += wv[3].y * x.w; }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (w0 + k >= nw) break;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                if (j == 1 && !has1) break;
+                float s = acc[k][j];
+                if (act == 0) s = tanhf(s);
+                else if (act == 1) s = s > 0.f ? s : expm1f(s);
+                out[(size_t)(w0 + k) * ostr + o0 + j] = s;
+            }
+        }
+    }
+}
+
+// Policy phase for the CTA's world block: obs -> normalise -> MLP -> sample -> writes.
+// Leaves the block's actions in actb[w][29].  k_rollout body, g1_env.cu:296-318.
+// final_value: only the value head is used (bootstrap Vlast, g1_env.cu:325-332).
+__device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, float* work, float* actb, int wbeg, int nbw, int t,
+                             bool final_value) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* X = work;  // [nbw][XSTR]
+    int maxw = 0;
+    for (int l = 0; l < P.nh; ++l) maxw = max(maxw, P.hid[l]);
+    const int hstr = ((maxw + 3) & ~3) + 4;
+    float* H0 = X + MAX_WB * XSTR;
+    float* H1 = H0 + MAX_WB * hstr;
+    // observations (raw to O, normalised to X)
+    for (int w = warp; w < nbw; w += NWARPS) {
+        const int gw = wbeg + w;
+        const float* qp = P.qp + (size_t)gw * NQ;
+        const float* qv = P.qv + (size_t)gw * NV;
+        const float* pa = P.pa + (size_t)gw * NU;
+        for (int i = lane; i < OBS_DIM; i += 32) {
+            float o = obs_elem(i, qp, qv, pa, T);
+            if (!final_value) P.O[((size_t)t * P.N + gw) * OBS_DIM + i] = o;
+            float z = (o - P.mean[i]) / sqrtf(P.var[i] + 1e-8f);
+            if (z < -10.f) z = -10.f; else if (z > 10.f) z = 10.f;
+            X[w * XSTR + i] = z;
+        }
+        if (lane < XSTR - OBS_DIM) X[w * XSTR + OBS_DIM + lane] = 0.f;
+    }
+    __syncthreads();
+    // hidden layers
+    const float* wp = P.WT;
+    const float* in = X;
+    int nin = OBS_DIM, istr = XSTR;
+    float* bufs[2] = {H0, H1};
+    for (int l = 0; l < P.nh; ++l) {
+        const int no = P.hid[l];
+        float* out = bufs[l & 1];
+        cta_dense(wp, no, wp + (size_t)nin * no, nin, no, in, istr, out, hstr, nbw, P.act);
+        wp += (size_t)nin * no + no;
+        in = out; nin = no; istr = hstr;
+        __syncthreads();
+    }
+    // heads: 29 means + value (+2 pad) -> scratch row of 32 in X (X is dead now)
+    float* HD = X;
+    cta_dense(wp, 32, wp + (size_t)nin * 32, nin, 30, in, istr, HD, 32, nbw, -1);
+    const float* lsp = wp + (size_t)nin * 32 + 32;
+    __syncthreads();
+    // sampling: one thread per world, actions in index order (g1_env.cu:308-314)
+    if (threadIdx.x < nbw) {
+        const int w = threadIdx.x, gw = wbeg + w;
+        const float* hd = HD + w * 32;
+        if (final_value) {
+            P.Vlast[gw] = hd[29];
+        } else {
+            const float LOG2PI = 1.8378770664093453f;
+            const uint64_t tick = P.tick0 + (uint64_t)t;
+            float lps = 0.f;
+            const size_t sb = (size_t)t * P.N + gw;
+            for (int i = 0; i < ACT_DIM; ++i) {
+                uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)gw, tick, RNG_ACTION, (uint32_t)i);
+                float nz = sqrtf(-2.f * logf(u01_open(rb.x))) * cosf(6.283185307179586f * u01(rb.y));
+                float ls = lsp[i];
+                float a = hd[i] + expf(ls) * nz;
+                lps += -0.5f * nz * nz - ls - 0.5f * LOG2PI;
+                actb[w * ACT_DIM + i] = a;
+                P.A[sb * ACT_DIM + i] = a;
+            }
+            P.LP[sb] = lps;
+            P.V[sb] = hd[29];
+        }
+    }
+    __syncthreads();
+}
+
+// ------------------------------------------------------------------ physics phase
+// One control step of one world by one warp: PD targets, S substeps, reward, done,
+// auto-reset.  env_advance, g1_env.cu:118-212.
+__device__ void warp_control_step(const Params& P, const G1Tables& T, float* fr, int gw, const float* a, uint64_t tick,
+                                  float* r_out, int* d_out) {
+    using L = FrameLayout;
+    const int lane = threadIdx.x & 31;
+    float *qp = fr + L::QP, *qv = fr + L::QV, *tgt = fr + L::TGT, *tau = fr + L::TAU;
+    float* misc = fr + L::MISC;
+    // load state
+    for (int i = lane; i < NQ; i += 32) qp[i] = P.qp[(size_t)gw * NQ + i];
+    for (int i = lane; i < NV; i += 32) qv[i] = P.qv[(size_t)gw * NV + i];
+    float pa_i = lane < ACT_DIM ? P.pa[(size_t)gw * NU + lane] : 0.f;
+    float a_i = lane < ACT_DIM ? a[lane] : 0.f;
+    if (lane < ACT_DIM) {
+        float t = T.target0[lane] + ACT_SCALE * a_i;
+        if (t < T.ctrl_lo[lane]) t = T.ctrl_lo[lane];
+        if (t > T.ctrl_hi[lane]) t = T.ctrl_hi[lane];
+        tgt[lane] = t;
+    }
+    if (lane < 6) tau[lane] = 0.f;
+    float energy = 0.f, vx_sum = 0.f;
+    __syncwarp();
+    QaccOpts opt;
+    opt.pgs_iters = P.pgs; opt.mu = P.mu; opt.bdt = T.bdt;
+    for (int s = 0; s < P.S; ++s) {
+        if (P.lockstep) asm volatile("bar.sync 1, %0;" ::"r"(NTHREADS) : "memory");
+#ifdef G1_PROF
+        long long _pt = clock64();
+#endif
+        float e = 0.f;
+        if (lane < ACT_DIM) {
+            int d = T.act_dof[lane];
+            float pdt = T.kp[lane] * (tgt[lane] - qp[T.act_qadr[lane]]) - T.kd[lane] * qv[d];
+            if (pdt < T.frc_lo[lane]) pdt = T.frc_lo[lane];
+            else if (pdt > T.frc_hi[lane]) pdt = T.frc_hi[lane];
+            tau[d] = pdt;
+            e = fabsf(pdt * qv[d]);
+        }
+        // energy accumulates actuator by actuator in index order (g1_env.cu:151)
+#pragma unroll
+        for (int i = 0; i < ACT_DIM; ++i) energy += __shfl_sync(FULLMASK, e, i);
+        __syncwarp();
+        PROF_MARK(P_STEP);
+        int ncon = warp_qacc(fr, T, lane, opt);
+        if (P.ncon_hist && lane == 0) atomicAdd(&P.ncon_hist[ncon], 1);
+        {
+            PROF_BEGIN();
+            warp_integrate(fr, T, lane, true);
+            vx_sum += qv[0];
+            PROF_MARK(P_STEP);
+        }
+    }
+    // reward / termination (g1_env.cu:164-197)
+    float vx = vx_sum / (float)P.S, height = qp[2];
+    float m[9];
+    qmat(ld4(qp + 3), m);
+    float up = m[8];
+    int alive = (height < 0.45f || up < 0.5f) ? 0 : 1;
+    float upc = up < 0.f ? 0.f : (up > 1.f ? 1.f : up);
+    float vxc = vx > CMD_VX ? CMD_VX : vx;
+    if (vxc < 0.f) vxc = 0.f;
+    float r_vel = 1.0f * vxc * upc;
+    float r_lat = -0.2f * fabsf(qv[1]) - 0.05f * fabsf(qv[5]);
+    float r_up = 0.3f * upc;
+    float r_h = -0.5f * fabsf(height - 0.78f);
+    float dai = a_i - pa_i, pterm = dai * dai;
+    float act_pen = 0.f;
+#pragma unroll
+    for (int i = 0; i < ACT_DIM; ++i) act_pen += __shfl_sync(FULLMASK, pterm, i);
+    if (act_pen > 10.f) act_pen = 10.f;
+    float r = alive ? 1.0f + r_vel + r_lat + r_up + r_h - 0.005f * act_pen - 1e-4f * energy : -5.0f;
+    int step = P.steps[gw] + 1;
+    int won = (alive && qp[0] >= X_FIN);
+    if (won) r += FINISH_BONUS;
+    int d_flag = (!alive || won || step >= 1000) ? 1 : 0;
+    __syncwarp();
+    float pa_new = a_i;
+    if (d_flag) {  // auto-reset (g1_env.cu:202-210)
+        for (int i = lane; i < NQ; i += 32) qp[i] = T.qpos_stand[i];
+        __syncwarp();
+        if (lane < ACT_DIM) {
+            uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)gw, tick, RNG_AUTORESET, (uint32_t)lane);
+            qp[T.act_qadr[lane]] += 0.05f * (u01_open(rb.x) * 2.f - 1.f);
+        }
+        for (int i = lane; i < NV; i += 32) qv[i] = 0.f;
+        pa_new = 0.f;
+        step = 0;
+    }
+    __syncwarp();
+    for (int i = lane; i < NQ; i += 32) P.qp[(size_t)gw * NQ + i] = qp[i];
+    for (int i = lane; i < NV; i += 32) P.qv[(size_t)gw * NV + i] = qv[i];
+    if (lane < ACT_DIM) P.pa[(size_t)gw * NU + lane] = pa_new;
+    if (lane == 0) P.steps[gw] = step;
+    (void)misc;
+    *r_out = r;
+    *d_out = d_flag;
+}
+
+// ------------------------------------------------------------------ the kernel
+struct SmemPlan {
+    int tab_floats, frame_floats, actb_floats, total_bytes;
+};
+__host__ __device__ inline SmemPlan smem_plan() {
+    SmemPlan p;
+    p.tab_floats = ((int)((sizeof(G1Tables) + 15) / 16)) * 4;
+    p.frame_floats = NWARPS * FRAME_FLOATS;
+    p.actb_floats = MAX_WB * ACT_DIM + 4;
+    p.total_bytes = (p.tab_floats + p.frame_floats + p.actb_floats) * 4;
+    return p;
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
+    extern __shared__ float4 smem4[];
+    float* smem = reinterpret_cast<float*>(smem4);
+    const SmemPlan plan = smem_plan();
+    {  // model tables -> shared memory
+        const int4* src = reinterpret_cast<const int4*>(&c_tab);
+        int4* dst = reinterpret_cast<int4*>(smem);
+        for (int i = threadIdx.x; i < (int)(sizeof(G1Tables) / 16); i += blockDim.x) dst[i] = src[i];
+    }
+    const G1Tables& T = *reinterpret_cast<const G1Tables*>(smem);
+    float* frames = smem + plan.tab_floats;
+    float* actb = frames + plan.frame_floats;
+    int* qctr = reinterpret_cast<int*>(actb + MAX_WB * ACT_DIM);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* fr = frames + warp * FRAME_FLOATS;
+    __syncthreads();
+
+    const int wbeg = blockIdx.x * P.wb;
+    const int nbw = min(P.wb, P.N - wbeg);
+    if (nbw <= 0) return;
+    const int nsteps = P.mode == MODE_ROLLOUT ? P.H : (P.mode == MODE_PHYS ? P.K : 1);
+    for (int t = 0; t < nsteps; ++t) {
+        const uint64_t tick = P.tick0 + (uint64_t)t;
+        PROF_BEGIN();
+        if (P.mode == MODE_ROLLOUT) {
+            policy_phase(P, T, frames, actb, wbeg, nbw, t, false);
+            PROF_MARK(P_POLICY);
+        } else {
+            for (int i = threadIdx.x; i < nbw * ACT_DIM; i += blockDim.x)
+                actb[i] = P.mode == MODE_STEP ? P.act_in[(size_t)wbeg * ACT_DIM + i] : 0.f;
+        }
+        if (threadIdx.x == 0) *qctr = 0;
+        __syncthreads();
+        // physics: warps pull worlds from the block queue (or, in lockstep mode, take worlds
+        // warp, warp+NWARPS, ... and idle through the substep barriers when out of worlds)
+        for (int round = 0;; ++round) {
+            int w = 0;
+            if (P.lockstep) {
+                if (round * NWARPS >= nbw) break;
+                w = warp + round * NWARPS;
+                if (w >= nbw) {
+                    for (int s = 0; s < P.S; ++s) asm volatile("bar.sync 1, %0;" ::"r"(NTHREADS) : "memory");
+                    continue;
+                }
+            } else {
+                if (lane == 0) w = atomicAdd(qctr, 1);
+                w = __shfl_sync(FULLMASK, w, 0);
+                if (w >= nbw) break;
+            }
+            const int gw = wbeg + w;
+            float r;
+            int d;
+            warp_control_step(P, T, fr, gw, actb + w * ACT_DIM, tick, &r, &d);
+            if (lane == 0) {
+                if (P.mode == MODE_ROLLOUT) {
+                    P.R[(size_t)t * P.N + gw] = r;
+                    P.D[(size_t)t * P.N + gw] = (float)d;
+                } else if (P.mode == MODE_STEP) {
+                    P.rew_out[gw] = r;
+                    P.done_out[gw] = (float)d;
+                }
+            }
+            if (P.mode == MODE_STEP) {  // k_step's obs after the step (g1_env.cu:265-266)
+                using L = FrameLayout;
+                __syncwarp();
+                const float* qp = P.qp + (size_t)gw * NQ;  // written back by this warp
+                const float* qv = P.qv + (size_t)gw * NV;
+                const float* pa = P.pa + (size_t)gw * NU;
+                __syncwarp();
+                for (int i = lane; i < OBS_DIM; i += 32) P.obs_out[(size_t)gw * OBS_DIM + i] = obs_elem(i, qp, qv, pa, T);
+                (void)sizeof(L);
+            }
+            __syncwarp();
+        }
+        {
+            PROF_BEGIN();
+            __syncthreads();
+            PROF_MARK(P_WAIT);
+        }
+    }
+    if (P.mode == MODE_ROLLOUT) policy_phase(P, T, frames, actb, wbeg, nbw, 0, true);
+}
+
+// Per-state FK + generalized acceleration (the reference's test_envqacc.cu harness
+// semantics, with caller states): one warp per state.
+__global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, const float* qvel, const float* tau,
+                                                      const float* bdt, int pgs, float mu, float* qacc_out,
+                                                      float* qacc_s_out, float* bias_out, float* f_out, int* ncon_out) {
+    extern __shared__ float4 smem4[];
+    float* smem = reinterpret_cast<float*>(smem4);
+    const SmemPlan plan = smem_plan();
+    {
+        const int4* src = reinterpret_cast<const int4*>(&c_tab);
+        int4* dst = reinterpret_cast<int4*>(smem);
+        for (int i = threadIdx.x; i < (int)(sizeof(G1Tables) / 16); i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    const G1Tables& T = *reinterpret_cast<const G1Tables*>(smem);
+    using L = FrameLayout;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* fr = smem + plan.tab_floats + warp * FRAME_FLOATS;
+    float* bd = smem + plan.tab_floats + plan.frame_floats + warp * 36;  // per-warp damping
+    for (int w = blockIdx.x * NWARPS + warp; w < n; w += gridDim.x * NWARPS) {
+        for (int i = lane; i < NQ; i += 32) fr[L::QP + i] = qpos[(size_t)w * NQ + i];
+        for (int i = lane; i < NV; i += 32) {
+            fr[L::QV + i] = qvel[(size_t)w * NV + i];
+            fr[L::TAU + i] = tau ? tau[(size_t)w * NV + i] : 0.f;
+            bd[i] = bdt ? bdt[(size_t)w * NV + i] : 0.f;
+        }
+        __syncwarp();
+        QaccOpts opt;
+        opt.pgs_iters = pgs; opt.mu = mu; opt.bdt = bd;
+        int ncon = warp_qacc(fr, T, lane, opt);
+        for (int i = lane; i < NV; i += 32) {
+            if (qacc_out) qacc_out[(size_t)w * NV + i] = fr[L::QACC + i];
+            if (qacc_s_out) qacc_s_out[(size_t)w * NV + i] = fr[L::MM + i];
+            if (bias_out) bias_out[(size_t)w * NV + i] = fr[L::BIAS + i];
+        }
+        if (f_out) f_out[(size_t)w * MAXEFC + lane] = lane < 4 * ncon ? fr[L::FF + lane] : 0.f;
+        if (ncon_out && lane == 0) ncon_out[w] = ncon;
+        __syncwarp();
+    }
+}
+
+// Reset: stand pose + U(+-0.02) joint noise (k_reset, g1_env.cu:97-111); obs optional.
+__global__ void k_reset(Params P, float* obs) {
+    const int w = blockIdx.x * blockDim.x + threadIdx.x;
+    if (w >= P.N) return;
+    G1Tables const& T = c_tab;
+    float* qp = P.qp + (size_t)w * NQ;
+    float* qv = P.qv + (size_t)w * NV;
+    float* pa = P.pa + (size_t)w * NU;
+    for (int i = 0; i < NQ; ++i) qp[i] = T.qpos_stand[i];
+    for (int i = 0; i < ACT_DIM; ++i) {
+        uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)w, P.tick0, RNG_RESET, (uint32_t)i);
+        qp[T.act_qadr[i]] += 0.02f * (u01_open(rb.x) * 2.f - 1.f);
+    }
+    for (int i = 0; i < NV; ++i) qv[i] = 0.f;
+    for (int i = 0; i < ACT_DIM; ++i) pa[i] = 0.f;
+    P.steps[w] = 0;
+    if (obs)
+        for (int i = 0; i < OBS_DIM; ++i) obs[(size_t)w * OBS_DIM + i] = obs_elem(i, qp, qv, pa, T);
+}
+
+// Repack the torch-ordered actor-critic weights (ppo_fused.py:35-44: per hidden layer
+// W[out,in], b; Wmu, bmu, Wv, bv, log_std) into the kernel layout (per layer W^T[in][out],
+// b; head W^T[nlast][32] with 29 mean rows + value row, b[32], log_std[32]).
+__global__ void k_repack(const float* W, float* WT, int nh, int h0, int h1, int h2, int h3) {
+    const int hid[4] = {h0, h1, h2, h3};
+    size_t src = 0, dst = 0;
+    int nin = OBS_DIM;
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
+    for (int l = 0; l < nh; ++l) {
+        const int no = hid[l];
+        for (size_t e = tid; e < (size_t)nin * no; e += nth) {
+            size_t o = e / nin, i = e % nin;
+            WT[dst + i * no + o] = W[src + e];
+        }
+        for (size_t e = tid; e < (size_t)no; e += nth) WT[dst + (size_t)nin * no + e] = W[src + (size_t)nin * no + e];
+        src += (size_t)nin * no + no;
+        dst += (size_t)nin * no + no;
+        nin = no;
+    }
+    // head
+    for (size_t e = tid; e < (size_t)nin * 32; e += nth) {
+        size_t i = e / 32, o = e % 32;
+        float v = 0.f;
+        if (o < ACT_DIM) v = W[src + o * nin + i];
+        else if (o == ACT_DIM) v = W[src + (size_t)ACT_DIM * nin + ACT_DIM + i];
+        WT[dst + e] = v;
+    }
+    for (size_t e = tid; e < 32; e += nth) {
+        float b = 0.f, ls = 0.f;
+        if (e < ACT_DIM) { b = W[src + (size_t)ACT_DIM * nin + e]; ls = W[src + (size_t)ACT_DIM * nin + ACT_DIM + nin + 1 + e]; }
+        else if (e == ACT_DIM) b = W[src + (size_t)ACT_DIM * nin + ACT_DIM + nin];
+        WT[dst + (size_t)nin * 32 + e] = b;
+        WT[dst + (size_t)nin * 32 + 32 + e] = ls;
+    }
+}
+
+// ------------------------------------------------------------------ host side
+struct EnvState {
+    int N, S, pgs, device;
+    float mu;
+    uint64_t seed;
+    uint32_t world0;
+    uint64_t tick;
+    float *qp, *qv, *pa;
+    int* steps;
+    float *dact, *dobs, *drew, *ddone;  // host-loop staging (g1_env.cu:88-89)
+    float* WT;                          // repacked policy weights
+    size_t WT_cap;
+    int nh, hid[MAX_HIDDEN], act;
+    int sm_count;
+    int* ncon_hist;
+    cudaStream_t stream;                // 0 = legacy default stream (the reference's)
+};
+
+static std::once_flag g_tab_once[64];
+static int upload_tables(int dev) {
+    int rc = 0;
+    std::call_once(g_tab_once[dev & 63], [&]() {
+        G1Tables T;
+        g1_build_tables(&T);
+        if (cudaMemcpyToSymbol(c_tab, &T, sizeof(T)) != cudaSuccess) rc = -1;
+        SmemPlan p = smem_plan();
+        if (cudaFuncSetAttribute(k_g1, cudaFuncAttributeMaxDynamicSharedMemorySize, p.total_bytes) != cudaSuccess) rc = -2;
+        if (cudaFuncSetAttribute(k_qacc, cudaFuncAttributeMaxDynamicSharedMemorySize, p.total_bytes) != cudaSuccess) rc = -3;
+    });
+    return rc;
+}
+
+static Params base_params(EnvState* E) {
+    Params P;
+    memset(&P, 0, sizeof P);
+    P.N = E->N; P.S = E->S; P.pgs = E->pgs; P.mu = E->mu;
+    P.qp = E->qp; P.qv = E->qv; P.pa = E->pa; P.steps = E->steps;
+    P.seed = E->seed; P.world0 = E->world0; P.tick0 = E->tick;
+    P.nh = E->nh; P.act = E->act;
+    for (int i = 0; i < MAX_HIDDEN; ++i) P.hid[i] = E->hid[i];
+    P.ncon_hist = E->ncon_hist;
+    P.lockstep = getenv("G1_LOCKSTEP") ? atoi(getenv("G1_LOCKSTEP")) : 1;
+    // worlds per CTA: spread over all SMs, at most MAX_WB (then CTAs run in waves)
+    int wb = (E->N + E->sm_count - 1) / E->sm_count;
+    if (wb > MAX_WB) wb = MAX_WB;
+    if (wb < 1) wb = 1;
+    P.wb = wb;
+    return P;
+}
+
+static bool launch_g1(EnvState* E, const Params& P) {
+    const int grid = (P.N + P.wb - 1) / P.wb;
+    const SmemPlan plan = smem_plan();
+    k_g1<<<grid, NTHREADS, plan.total_bytes, E->stream>>>(P);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_error((int)e, "k_g1 launch", cudaGetErrorString(e)); return false; }
+    return true;
+}
+
+static size_t policy_floats(int nh, const int* hid) {
+    size_t n = 0;
+    int nin = OBS_DIM;
+    for (int l = 0; l < nh; ++l) { n += (size_t)nin * hid[l] + hid[l]; nin = hid[l]; }
+    return n + (size_t)nin * 32 + 64;
+}
+
+extern "C" {
+
+const char* g1_env_last_error(void) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    return g_last_code ? g_last_error.c_str() : nullptr;
+}
+int g1_env_last_error_code(void) { return g_last_code; }
+void g1_env_clear_error(void) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    g_last_code = 0;
+    g_last_error.clear();
+}
+
+int g1_env_obs_dim(void) { return OBS_DIM; }
+int g1_env_act_dim(void) { return ACT_DIM; }
+
+void* g1_env_create_ex(int N, int substeps, int pgs_iters, unsigned long seed, int device, unsigned int world0, float mu) {
+    if (N <= 0 || substeps <= 0 || pgs_iters < 0) { set_error(-22, "g1_env_create", "invalid argument"); return nullptr; }
+    if (device >= 0) CKR(cudaSetDevice(device), nullptr);
+    int dev = 0;
+    CKR(cudaGetDevice(&dev), nullptr);
+    if (upload_tables(dev) != 0) { set_error(-1, "g1_env_create", "table upload / smem attribute failed"); return nullptr; }
+    EnvState* E = new EnvState();
+    memset(E, 0, sizeof *E);
+    E->N = N; E->S = substeps; E->pgs = pgs_iters; E->device = dev; E->seed = seed; E->world0 = world0; E->mu = mu;
+    E->nh = 2; E->hid[0] = 256; E->hid[1] = 256; E->act = 0;  // the reference's AC (ppo.py:85-99)
+    cudaDeviceGetAttribute(&E->sm_count, cudaDevAttrMultiProcessorCount, dev);
+    bool ok = cudaMalloc(&E->qp, (size_t)N * NQ * 4) == cudaSuccess && cudaMalloc(&E->qv, (size_t)N * NV * 4) == cudaSuccess &&
+              cudaMalloc(&E->pa, (size_t)N * NU * 4) == cudaSuccess && cudaMalloc(&E->steps, (size_t)N * 4) == cudaSuccess &&
+              cudaMalloc(&E->dact, (size_t)N * ACT_DIM * 4) == cudaSuccess &&
+              cudaMalloc(&E->dobs, (size_t)N * OBS_DIM * 4) == cudaSuccess && cudaMalloc(&E->drew, (size_t)N * 4) == cudaSuccess &&
+              cudaMalloc(&E->ddone, (size_t)N * 4) == cudaSuccess;
+    if (!ok) {
+        set_error(2, "g1_env_create", "cudaMalloc failed");
+        cudaFree(E->qp); cudaFree(E->qv); cudaFree(E->pa); cudaFree(E->steps);
+        cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone);
+        delete E;
+        return nullptr;
+    }
+    // a valid state before the first reset: the stand pose without noise
+    Params P = base_params(E);
+    k_reset<<<(N + 127) / 128, 128>>>(P, nullptr);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { set_error((int)e, "g1_env_create", cudaGetErrorString(e)); }
+    return E;
+}
+
+// g1_env.cu:405-422
+void* g1_env_create(int N, int substeps, int pgs_iters, unsigned long seed) {
+    return g1_env_create_ex(N, substeps, pgs_iters, seed, -1, 0u, G1M_FOOT_MU_MODEL);
+}
+
+void g1_env_destroy(void* h) {  // g1_env.cu:469-474
+    EnvState* E = (EnvState*)h;
+    if (!E) return;
+    cudaFree(E->qp); cudaFree(E->qv); cudaFree(E->pa); cudaFree(E->steps);
+    cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone);
+    cudaFree(E->WT); cudaFree(E->ncon_hist);
+    delete E;
+}
+
+void g1_env_set_stream(void* h, void* stream) { ((EnvState*)h)->stream = (cudaStream_t)stream; }
+
+int g1_env_set_policy(void* h, int nh, const int* hidden, int activation) {
+    EnvState* E = (EnvState*)h;
+    if (nh < 1 || nh > MAX_HIDDEN || activation < 0 || activation > 1) { set_error(-22, "g1_env_set_policy", "invalid"); return -22; }
+    for (int i = 0; i < nh; ++i)
+        if (hidden[i] < 1 || hidden[i] > 1024 || (hidden[i] & 1)) { set_error(-22, "g1_env_set_policy", "bad width"); return -22; }
+    // MLP activations for MAX_WB worlds must fit in the physics frames it aliases
+    int maxw = 0;
+    for (int i = 0; i < nh; ++i) maxw = hidden[i] > maxw ? hidden[i] : maxw;
+    size_t need = (size_t)MAX_WB * XSTR + 2 * (size_t)MAX_WB * (((maxw + 3) & ~3) + 4);
+    if (need > (size_t)NWARPS * FRAME_FLOATS) { set_error(-22, "g1_env_set_policy", "hidden width too large for this build"); return -22; }
+    E->nh = nh; E->act = activation;
+    for (int i = 0; i < MAX_HIDDEN; ++i) E->hid[i] = i < nh ? hidden[i] : 0;
+    return 0;
+}
+
+void g1_env_set_friction(void* h, float mu) { ((EnvState*)h)->mu = mu; }
+
+// g1_env.cu:424-429 (host obs_out [N x 100], synchronous)
+void g1_env_reset(void* h, float* obs_out) {
+    EnvState* E = (EnvState*)h;
+    Params P = base_params(E);
+    k_reset<<<(E->N + 127) / 128, 128, 0, E->stream>>>(P, E->dobs);
+    CKR(cudaGetLastError(), );
+    if (obs_out) CKR(cudaMemcpyAsync(obs_out, E->dobs, (size_t)E->N * OBS_DIM * 4, cudaMemcpyDeviceToHost, E->stream), );
+    CKR(cudaStreamSynchronize(E->stream), );
+}
+
+// g1_env.cu:431-441 (host pointers; synchronous).  Advances the control tick.
+void g1_env_step(void* h, const float* act, float* obs, float* rew, float* done) {
+    EnvState* E = (EnvState*)h;
+    CKR(cudaMemcpyAsync(E->dact, act, (size_t)E->N * ACT_DIM * 4, cudaMemcpyHostToDevice, E->stream), );
+    Params P = base_params(E);
+    P.mode = MODE_STEP;
+    P.act_in = E->dact; P.obs_out = E->dobs; P.rew_out = E->drew; P.done_out = E->ddone;
+    if (!launch_g1(E, P)) return;
+    E->tick += 1;
+    CKR(cudaMemcpyAsync(obs, E->dobs, (size_t)E->N * OBS_DIM * 4, cudaMemcpyDeviceToHost, E->stream), );
+    CKR(cudaMemcpyAsync(rew, E->drew, (size_t)E->N * 4, cudaMemcpyDeviceToHost, E->stream), );
+    CKR(cudaMemcpyAsync(done, E->ddone, (size_t)E->N * 4, cudaMemcpyDeviceToHost, E->stream), );
+    CKR(cudaStreamSynchronize(E->stream), );
+}
+
+// Device-pointer variant of g1_env_step (no host copies, asynchronous on the env stream).
+void g1_env_step_device(void* h, const float* act, float* obs, float* rew, float* done) {
+    EnvState* E = (EnvState*)h;
+    Params P = base_params(E);
+    P.mode = MODE_STEP;
+    P.act_in = act; P.obs_out = obs; P.rew_out = rew; P.done_out = done;
+    if (launch_g1(E, P)) E->tick += 1;
+}
+
+// g1_env.cu:446-453: the fused rollout into caller-owned DEVICE buffers, asynchronous.
+void g1_rollout(void* h, int H, const float* W, const float* mean, const float* var, float* O, float* A, float* LP,
+                float* V, float* R, float* D, float* Vlast) {
+    EnvState* E = (EnvState*)h;
+    if (H <= 0) return;
+    size_t need = policy_floats(E->nh, E->hid);
+    if (need > E->WT_cap) {
+        cudaFree(E->WT);
+        E->WT = nullptr;
+        CKR(cudaMalloc(&E->WT, need * 4), );
+        E->WT_cap = need;
+    }
+    k_repack<<<120, 256, 0, E->stream>>>(W, E->WT, E->nh, E->hid[0], E->hid[1], E->hid[2], E->hid[3]);
+    CKR(cudaGetLastError(), );
+    Params P = base_params(E);
+    P.mode = MODE_ROLLOUT; P.H = H;
+    P.WT = E->WT; P.mean = mean; P.var = var;
+    P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
+    if (launch_g1(E, P)) E->tick += (uint64_t)H;
+}
+
+// g1_env.cu:385-389: K control steps with zero action, synchronous.
+void g1_env_bench_phys(void* h, int K) {
+    EnvState* E = (EnvState*)h;
+    if (K <= 0) return;
+    Params P = base_params(E);
+    P.mode = MODE_PHYS; P.K = K;
+    if (!launch_g1(E, P)) return;
+    E->tick += (uint64_t)K;
+    CKR(cudaStreamSynchronize(E->stream), );
+}
+
+// Asynchronous variant of g1_env_bench_phys (for timing with events on the env stream).
+void g1_env_phys_async(void* h, int K) {
+    EnvState* E = (EnvState*)h;
+    if (K <= 0) return;
+    Params P = base_params(E);
+    P.mode = MODE_PHYS; P.K = K;
+    if (launch_g1(E, P)) E->tick += (uint64_t)K;
+}
+
+// g1_env.cu:457-467
+void g1_env_qpos(void* h, float* out) {
+    EnvState* E = (EnvState*)h;
+    CKR(cudaMemcpyAsync(out, E->qp, (size_t)NQ * 4, cudaMemcpyDeviceToHost, E->stream), );
+    CKR(cudaStreamSynchronize(E->stream), );
+}
+void g1_env_qpos_all(void* h, float* out) {
+    EnvState* E = (EnvState*)h;
+    CKR(cudaMemcpyAsync(out, E->qp, (size_t)E->N * NQ * 4, cudaMemcpyDeviceToHost, E->stream), );
+    CKR(cudaStreamSynchronize(E->stream), );
+}
+
+// Host state access (for checkpoint/parity): qp [N*36], qv [N*35], pa [N*29] float,
+// steps [N] int, tick.  Any pointer may be null.  Synchronous.
+void g1_env_get_state(void* h, float* qp, float* qv, float* pa, int* steps, unsigned long long* tick) {
+    EnvState* E = (EnvState*)h;
+    if (qp) CKR(cudaMemcpyAsync(qp, E->qp, (size_t)E->N * NQ * 4, cudaMemcpyDeviceToHost, E->stream), );
+    if (qv) CKR(cudaMemcpyAsync(qv, E->qv, (size_t)E->N * NV * 4, cudaMemcpyDeviceToHost, E->stream), );
+    if (pa) CKR(cudaMemcpyAsync(pa, E->pa, (size_t)E->N * NU * 4, cudaMemcpyDeviceToHost, E->stream), );
+    if (steps) CKR(cudaMemcpyAsync(steps, E->steps, (size_t)E->N * 4, cudaMemcpyDeviceToHost, E->stream), );
+    CKR(cudaStreamSynchronize(E->stream), );
+    if (tick) *tick = E->tick;
+}
+void g1_env_set_state(void* h, const float* qp, const float* qv, const float* pa, const int* steps, unsigned long long tick) {
+    EnvState* E = (EnvState*)h;
+    if (qp) CKR(cudaMemcpyAsync(E->qp, qp, (size_t)E->N * NQ * 4, cudaMemcpyHostToDevice, E->stream), );
+    if (qv) CKR(cudaMemcpyAsync(E->qv, qv, (size_t)E->N * NV * 4, cudaMemcpyHostToDevice, E->stream), );
+    if (pa) CKR(cudaMemcpyAsync(E->pa, pa, (size_t)E->N * NU * 4, cudaMemcpyHostToDevice, E->stream), );
+    if (steps) CKR(cudaMemcpyAsync(E->steps, steps, (size_t)E->N * 4, cudaMemcpyHostToDevice, E->stream), );
+    CKR(cudaStreamSynchronize(E->stream), );
+    E->tick = tick;
+}
+
+// Contact-count histogram over all substeps since enabled (ncon 0..8), for the roofline
+// FLOP tally.  enable=1 allocates/zeroes, enable=0 disables.  out[9] host.
+void g1_env_ncon_hist(void* h, int enable, unsigned long long* out) {
+    EnvState* E = (EnvState*)h;
+    if (out && E->ncon_hist) {
+        int tmp[MAXCON + 1];
+        CKR(cudaMemcpyAsync(tmp, E->ncon_hist, sizeof tmp, cudaMemcpyDeviceToHost, E->stream), );
+        CKR(cudaStreamSynchronize(E->stream), );
+        for (int i = 0; i <= MAXCON; ++i) out[i] = (unsigned long long)tmp[i];
+    }
+    if (enable) {
+        if (!E->ncon_hist) CKR(cudaMalloc(&E->ncon_hist, (MAXCON + 1) * sizeof(int)), );
+        CKR(cudaMemsetAsync(E->ncon_hist, 0, (MAXCON + 1) * sizeof(int), E->stream), );
+    } else if (E->ncon_hist) {
+        cudaFree(E->ncon_hist);
+        E->ncon_hist = nullptr;
+    }
+}
+
+// Per-state FK + generalized acceleration on DEVICE buffers (the per-substep parity gate;
+// test_envqacc.cu:29-51 semantics with caller states).  Outputs may be null.  Synchronous.
+int g1_qacc_batch(int n, const float* qpos, const float* qvel, const float* tau, const float* bdt, int pgs_iters, float mu,
+                  float* qacc, float* qacc_smooth, float* bias, float* f, int* ncon) {
+    int dev = 0;
+    CKR(cudaGetDevice(&dev), -1);
+    if (upload_tables(dev) != 0) { set_error(-1, "g1_qacc_batch", "table upload failed"); return -1; }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const SmemPlan plan = smem_plan();
+    int grid = (n + NWARPS - 1) / NWARPS;
+    if (grid > sms * 4) grid = sms * 4;
+    if (grid < 1) grid = 1;
+    k_qacc<<<grid, NTHREADS, plan.total_bytes>>>(n, qpos, qvel, tau, bdt, pgs_iters, mu, qacc, qacc_smooth, bias, f, ncon);
+    CKR(cudaGetLastError(), -1);
+    CKR(cudaDeviceSynchronize(), -1);
+    return 0;
+}
+
+// extension (profiling builds only, -DG1_PROF): per-phase warp cycles since the last call.
+int g1_prof_read(unsigned long long* out) {
+#ifdef G1_PROF
+    CKR(cudaDeviceSynchronize(), -1);
+    CKR(cudaMemcpyFromSymbol(out, g_prof, sizeof(unsigned long long) * 16), -1);
+    unsigned long long z[16] = {0};
+    CKR(cudaMemcpyToSymbol(g_prof, z, sizeof z), -1);
+    return 0;
+#else
+    (void)out;
+    return -1;
+#endif
+}
+
+// g1_env.cu:365-382
+void g1_occupancy_report(void) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, 0) != cudaSuccess) return;
+    printf("SM count %d, regs/SM %d, smem/SM %zu, maxThreads/SM %d\n", p.multiProcessorCount, p.regsPerMultiprocessor,
+           p.sharedMemPerMultiprocessor, p.maxThreadsPerMultiProcessor);
+    struct { const char* nm; const void* fn; } ks[] = {{"k_g1", (const void*)k_g1}, {"k_qacc", (const void*)k_qacc}};
+    const SmemPlan plan = smem_plan();
+    for (auto& k : ks) {
+        cudaFuncAttributes fa;
+        cudaFuncGetAttributes(&fa, k.fn);
+        int mb = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&mb, k.fn, NTHREADS, plan.total_bytes);
+        printf("  %-8s regs=%d localFrame=%zuB smem=%dB maxActiveBlocks/SM=%d warps/SM=%d\n", k.nm, fa.numRegs,
+               fa.localSizeBytes, plan.total_bytes, mb, mb * NWARPS);
+    }
+}
+
+}  // extern "C"

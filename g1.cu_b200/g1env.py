@@ -1,0 +1,293 @@
+"""Python host side of the B200 G1 rollout: the ctypes binding of libg1env.so plus the
+trainer-facing classes, under the names the reference's scripts use
+(scripts/ppo.py:24-125: the ctypes binding, G1Env, RunNorm, AC, evaluate;
+scripts/ppo_fused.py:27-44: the g1_rollout binding and pack_weights).
+
+The CUDA library is required: importing works on a CPU-only machine, but creating an env
+or calling a kernel entry point raises if libg1env.so is missing or no GPU is visible --
+there is no CPU fallback.
+"""
+import ctypes
+import os
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "libg1env.so")
+OBS_DIM, ACT_DIM, NQ, NV = 100, 29, 36, 35
+
+_fp = ctypes.POINTER(ctypes.c_float)
+_vp = ctypes.c_void_p
+_lib = None
+
+# exported symbols and their ctypes signatures (include/g1env.h)
+SIGNATURES = {
+    "g1_env_create": (_vp, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_ulong]),
+    "g1_env_create_ex": (_vp, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_ulong, ctypes.c_int, ctypes.c_uint,
+                               ctypes.c_float]),
+    "g1_env_destroy": (None, [_vp]),
+    "g1_env_reset": (None, [_vp, _fp]),
+    "g1_env_step": (None, [_vp, _fp, _fp, _fp, _fp]),
+    "g1_env_step_device": (None, [_vp] + [_vp] * 4),
+    "g1_rollout": (None, [_vp, ctypes.c_int] + [_vp] * 10),
+    "g1_env_bench_phys": (None, [_vp, ctypes.c_int]),
+    "g1_env_phys_async": (None, [_vp, ctypes.c_int]),
+    "g1_env_qpos": (None, [_vp, _fp]),
+    "g1_env_qpos_all": (None, [_vp, _fp]),
+    "g1_env_obs_dim": (ctypes.c_int, []),
+    "g1_env_act_dim": (ctypes.c_int, []),
+    "g1_occupancy_report": (None, []),
+    "g1_env_last_error": (ctypes.c_char_p, []),
+    "g1_env_last_error_code": (ctypes.c_int, []),
+    "g1_env_clear_error": (None, []),
+    "g1_env_set_stream": (None, [_vp, _vp]),
+    "g1_env_set_policy": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int]),
+    "g1_env_set_friction": (None, [_vp, ctypes.c_float]),
+    "g1_env_get_state": (None, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "g1_env_set_state": (None, [_vp, _vp, _vp, _vp, _vp, ctypes.c_ulonglong]),
+    "g1_env_ncon_hist": (None, [_vp, ctypes.c_int, _vp]),
+    "g1_qacc_batch": (ctypes.c_int, [ctypes.c_int] + [_vp] * 4 + [ctypes.c_int, ctypes.c_float] + [_vp] * 5),
+}
+
+
+class G1Error(RuntimeError):
+    pass
+
+
+def load_library(path=LIB):
+    """Load libg1env.so and bind every exported symbol (raises if it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise G1Error(f"{path} not built: run `python g1.cu_b200/build.py` (nvcc, sm_100a); "
+                      "there is no CPU fallback")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        f = getattr(lib, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _check():
+    code = _lib.g1_env_last_error_code()
+    if code:
+        msg = _lib.g1_env_last_error()
+        _lib.g1_env_clear_error()
+        raise G1Error(f"libg1env: {msg.decode() if msg else code}")
+
+
+def _p(a):
+    return a.ctypes.data_as(_fp)
+
+
+def _dp(t):
+    """device (or host numpy) pointer as c_void_p (ppo_fused.py:31-32)"""
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(_vp)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _require_gpu():
+    if not torch.cuda.is_available():
+        raise G1Error("no CUDA device visible: the G1 rollout runs only on the GPU (no CPU fallback)")
+
+
+class G1Env:
+    """Batched G1 env on one GPU (ppo.py:39-60).  All N worlds stay resident on the device."""
+
+    def __init__(self, n_worlds, substeps=10, pgs_iters=2000, seed=0, device=None, world0=0, mu=0.6):
+        _require_gpu()
+        lib = load_library()
+        self.N = n_worlds
+        self.obs_dim = lib.g1_env_obs_dim()
+        self.act_dim = lib.g1_env_act_dim()
+        dev = torch.cuda.current_device() if device is None else int(device)
+        self.device = dev
+        self.h = lib.g1_env_create_ex(n_worlds, substeps, pgs_iters, seed, dev, world0, mu)
+        if not self.h:
+            _check()
+            raise G1Error("g1_env_create failed")
+        self._obs = np.zeros((n_worlds, self.obs_dim), np.float32)
+        self._rew = np.zeros(n_worlds, np.float32)
+        self._done = np.zeros(n_worlds, np.float32)
+
+    def reset(self):
+        _lib.g1_env_reset(self.h, _p(self._obs)); _check()
+        return self._obs.copy()
+
+    def step(self, act):
+        act = np.ascontiguousarray(act, np.float32)
+        _lib.g1_env_step(self.h, _p(act), _p(self._obs), _p(self._rew), _p(self._done)); _check()
+        return self._obs.copy(), self._rew.copy(), self._done.copy()
+
+    def set_stream(self, stream):
+        _lib.g1_env_set_stream(self.h, ctypes.c_void_p(stream.cuda_stream if stream is not None else 0))
+
+    def set_policy(self, hidden=(256, 256), activation="tanh"):
+        hid = np.ascontiguousarray(hidden, np.int32)
+        rc = _lib.g1_env_set_policy(self.h, len(hidden), _dp(hid), 0 if activation == "tanh" else 1)
+        if rc:
+            _check()
+
+    def set_friction(self, mu):
+        _lib.g1_env_set_friction(self.h, float(mu))
+
+    def rollout(self, H, W, mean, var, O, A, LP, V, R, D, Vlast):
+        """g1_rollout on torch-owned device tensors (ppo_fused.py:101-102)."""
+        _lib.g1_rollout(self.h, H, _dp(W), _dp(mean), _dp(var), _dp(O), _dp(A), _dp(LP), _dp(V), _dp(R), _dp(D),
+                        _dp(Vlast))
+        _check()
+
+    def bench_phys(self, K):
+        _lib.g1_env_bench_phys(self.h, K); _check()
+
+    def phys_async(self, K):
+        _lib.g1_env_phys_async(self.h, K); _check()
+
+    def get_state(self):
+        N = self.N
+        qp = np.zeros((N, NQ), np.float32); qv = np.zeros((N, NV), np.float32); pa = np.zeros((N, ACT_DIM), np.float32)
+        st = np.zeros(N, np.int32); tick = np.zeros(1, np.uint64)
+        _lib.g1_env_get_state(self.h, _dp(qp), _dp(qv), _dp(pa), _dp(st), _dp(tick)); _check()
+        return qp, qv, pa, st, int(tick[0])
+
+    def set_state(self, qp, qv, pa, steps, tick=0):
+        N = self.N
+        a = [np.ascontiguousarray(qp, np.float32).reshape(N, NQ), np.ascontiguousarray(qv, np.float32).reshape(N, NV),
+             np.ascontiguousarray(pa, np.float32).reshape(N, ACT_DIM), np.ascontiguousarray(steps, np.int32).reshape(N)]
+        _lib.g1_env_set_state(self.h, *[_dp(x) for x in a], int(tick)); _check()
+
+    def qpos(self):
+        out = np.zeros(NQ, np.float32)
+        _lib.g1_env_qpos(self.h, _p(out)); _check()
+        return out
+
+    def qpos_all(self):
+        out = np.zeros((self.N, NQ), np.float32)
+        _lib.g1_env_qpos_all(self.h, _p(out)); _check()
+        return out
+
+    def ncon_hist(self, enable=True):
+        out = np.zeros(9, np.uint64)
+        _lib.g1_env_ncon_hist(self.h, 1 if enable else 0, _dp(out)); _check()
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            _lib.g1_env_destroy(self.h)
+            self.h = None
+
+
+def qacc_batch(qpos, qvel, tau=None, bdt=None, pgs_iters=8, mu=0.6):
+    """Per-state FK + generalized acceleration on the GPU (g1_qacc_batch).  Takes CUDA
+    tensors; returns dict of CUDA tensors qacc, qacc_smooth, bias [n,35], f [n,32], ncon [n]."""
+    _require_gpu()
+    lib = load_library()
+    n = qpos.shape[0]
+    dev = qpos.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    out = dict(qacc=torch.zeros(n, NV, **f32), qacc_smooth=torch.zeros(n, NV, **f32), bias=torch.zeros(n, NV, **f32),
+               f=torch.zeros(n, 32, **f32), ncon=torch.zeros(n, dtype=torch.int32, device=dev))
+    qpos = qpos.contiguous().float(); qvel = qvel.contiguous().float()
+    tau = None if tau is None else tau.contiguous().float()
+    bdt = None if bdt is None else bdt.expand(n, NV).contiguous().float()
+    rc = lib.g1_qacc_batch(n, _dp(qpos), _dp(qvel), _dp(tau), _dp(bdt), pgs_iters, float(mu),
+                           *[_dp(out[k]) for k in ("qacc", "qacc_smooth", "bias", "f", "ncon")])
+    if rc:
+        _check()
+    return out
+
+
+# ---------------- running obs normalizer (ppo.py:63-81) ----------------
+class RunNorm:
+    """Running mean/var of observations (clipped normalisation)."""
+
+    def __init__(self, dim, dev):
+        self.mean = torch.zeros(dim, device=dev)
+        self.var = torch.ones(dim, device=dev)
+        self.count = 1e-4
+
+    def update_from_moments(self, bm, bv, b):
+        tot = self.count + b
+        delta = bm - self.mean
+        self.mean = self.mean + delta * b / tot
+        self.var = (self.var * self.count + bv * b + delta ** 2 * self.count * b / tot) / tot
+        self.count = tot
+
+    def update(self, x):  # x: [B, dim]
+        self.update_from_moments(x.mean(0), x.var(0, unbiased=False), x.shape[0])
+
+    def norm(self, x):
+        return torch.clamp((x - self.mean) / torch.sqrt(self.var + 1e-8), -10.0, 10.0)
+
+
+# ---------------- actor-critic (ppo.py:85-99) ----------------
+class AC(nn.Module):
+    def __init__(self, obs_dim, act_dim, hidden=(256, 256), activation="tanh"):
+        super().__init__()
+        layers, d = [], obs_dim
+        for h in hidden:
+            layers += [nn.Linear(d, h), nn.Tanh() if activation == "tanh" else nn.ELU()]
+            d = h
+        self.hidden = tuple(hidden)
+        self.activation = activation
+        self.body = nn.Sequential(*layers)
+        self.mu = nn.Linear(d, act_dim)
+        self.v = nn.Linear(d, 1)
+        self.log_std = nn.Parameter(-0.5 * torch.ones(act_dim))
+
+    def forward(self, x):
+        z = self.body(x)
+        return self.mu(z), self.log_std.exp(), self.v(z).squeeze(-1)
+
+
+def pack_weights(ac):
+    """Flatten AC params in the order the kernel unpacks (ppo_fused.py:35-44): per hidden
+    layer W,b; then Wmu,bmu, Wv,bv, log_std.  nn.Linear weight is [out,in] row-major."""
+    parts = []
+    for m in ac.body:
+        if isinstance(m, nn.Linear):
+            parts += [m.weight.reshape(-1), m.bias]
+    parts += [ac.mu.weight.reshape(-1), ac.mu.bias, ac.v.weight.reshape(-1), ac.v.bias, ac.log_std]
+    return torch.cat(parts).contiguous()
+
+
+def init_policy_normal(ac, seed=0):
+    """Config-2 style random init: N(0, 1/fan_in) weights, zero bias, log_std = -0.5."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    with torch.no_grad():
+        for m in ac.modules():
+            if isinstance(m, nn.Linear):
+                m.weight.copy_(torch.randn(m.weight.shape, generator=g) / np.sqrt(m.weight.shape[1]))
+                m.bias.zero_()
+        ac.log_std.fill_(-0.5)
+    return ac
+
+
+@torch.no_grad()
+def evaluate(env, ac, norm, dev, steps=200):
+    """Deterministic (mean) policy roll through the host-loop step path (ppo.py:103-125)."""
+    obs = torch.tensor(env.reset(), device=dev)
+    N = env.N
+    dt_ctrl = 0.02
+    fwd = np.zeros(N); alive_len = np.zeros(N); done_any = np.zeros(N, bool)
+    vx_acc = np.zeros(N)
+    for _ in range(steps):
+        mu, _, _ = ac(norm.norm(obs))
+        no, rw, dn = env.step(mu.cpu().numpy())
+        vx = no[:, 0]
+        live = ~done_any
+        fwd[live] += vx[live] * dt_ctrl
+        vx_acc[live] += vx[live]
+        alive_len[live] += 1
+        done_any |= dn.astype(bool)
+        obs = torch.tensor(no, device=dev)
+    return dict(fwd_mean=float(fwd.mean()), fwd_max=float(fwd.max()), ep_len_mean=float(alive_len.mean()),
+                fall_rate=float(done_any.mean()), vx_mean=float((vx_acc / np.maximum(alive_len, 1)).mean()))

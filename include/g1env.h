@@ -1,0 +1,107 @@
+/*
+ * g1env.h -- C-ABI of libg1env.so, the B200 (sm_100a) fused G1 rollout.
+ *
+ * Drop-in for the reference's ctypes library build/libg1env.so (Infatoshi/g1.cu,
+ * src/g1_env.cu:361-476): every reference export keeps its name, argument types, buffer
+ * layouts and ownership, so scripts/ppo.py and scripts/ppo_fused.py bind it unchanged.
+ * Additions (g1_env_*_ex / _device / _last_error / state access / g1_qacc_batch) are
+ * marked "extension".
+ *
+ * Conventions (as the reference):
+ *   - N worlds; OBS = 100, ACT = 29; NQ = 36, NV = 35 (MuJoCo qpos/qvel order).
+ *   - Trajectory buffers are world-major rows: O[H,N,100], A[H,N,29], LP/V/R/D[H,N],
+ *     Vlast[N], float32, done flags stored as 0.0/1.0.
+ *   - Policy weights W: one float32 buffer in torch parameter order, per hidden layer
+ *     W[out,in] row-major then bias; then Wmu[29,h], bmu[29], Wv[1,h], bv[1], log_std[29]
+ *     (ppo_fused.py:35-44).
+ *   - Errors: functions keep the reference's void returns; a failure is recorded and can be
+ *     read with g1_env_last_error() (the reference prints and calls exit(1),
+ *     g1_env.cu:33-34).  Functions returning int return 0 on success.
+ */
+#ifndef G1ENV_H
+#define G1ENV_H
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* replaces g1_env_create, g1_env.cu:405-422.  Allocates device state on the current
+ * device and places every world at the stand pose; returns NULL on failure. */
+void* g1_env_create(int n_worlds, int substeps, int pgs_iters, unsigned long seed);
+
+/* extension: explicit device ordinal (-1 = current), global id of world 0 (world shards of
+ * a multi-GPU job draw disjoint RNG streams), and foot friction mu (the reference
+ * hard-codes 0.6 in g1_model.h:420). */
+void* g1_env_create_ex(int n_worlds, int substeps, int pgs_iters, unsigned long seed, int device,
+                       unsigned int world0, float mu);
+
+/* replaces g1_env_destroy, g1_env.cu:469-474 */
+void g1_env_destroy(void* h);
+
+/* replaces g1_env_reset, g1_env.cu:424-429.  obs_out: HOST [N*100] (may be NULL). */
+void g1_env_reset(void* h, float* obs_out);
+
+/* replaces g1_env_step, g1_env.cu:431-441.  HOST pointers: act [N*29] -> obs [N*100],
+ * rew [N], done [N]; synchronous. */
+void g1_env_step(void* h, const float* act, float* obs, float* rew, float* done);
+
+/* extension: g1_env_step on DEVICE pointers, asynchronous on the env stream. */
+void g1_env_step_device(void* h, const float* act, float* obs, float* rew, float* done);
+
+/* replaces g1_rollout, g1_env.cu:446-453.  DEVICE pointers (torch-owned); asynchronous on
+ * the env stream (default: the legacy default stream, as the reference). */
+void g1_rollout(void* h, int H, const float* W, const float* mean, const float* var, float* O, float* A,
+                float* LP, float* V, float* R, float* D, float* Vlast);
+
+/* replaces g1_env_bench_phys, g1_env.cu:385-389: K control steps with zero action, synchronous. */
+void g1_env_bench_phys(void* h, int K);
+
+/* extension: asynchronous g1_env_bench_phys (timing with events on the env stream). */
+void g1_env_phys_async(void* h, int K);
+
+/* replaces g1_env_qpos / g1_env_qpos_all, g1_env.cu:457-467 (HOST out [36] / [N*36]). */
+void g1_env_qpos(void* h, float* out);
+void g1_env_qpos_all(void* h, float* out);
+
+/* replaces g1_env_obs_dim / g1_env_act_dim, g1_env.cu:391-392 */
+int g1_env_obs_dim(void);
+int g1_env_act_dim(void);
+
+/* replaces g1_occupancy_report, g1_env.cu:365-382 (prints) */
+void g1_occupancy_report(void);
+
+/* extension: error reporting in place of exit(1).  NULL / 0 when no error is pending. */
+const char* g1_env_last_error(void);
+int g1_env_last_error_code(void);
+void g1_env_clear_error(void);
+
+/* extension: stream for all asynchronous work of this env (a cudaStream_t; NULL = legacy default). */
+void g1_env_set_stream(void* h, void* stream);
+
+/* extension: policy architecture used by g1_rollout: nh hidden layers (1..4, even widths
+ * <= 1024), activation 0 = tanh (the reference's AC, ppo.py:85-99), 1 = ELU. */
+int g1_env_set_policy(void* h, int nh, const int* hidden, int activation);
+
+/* extension: foot friction coefficient mu of the pyramidal cone (default 0.6). */
+void g1_env_set_friction(void* h, float mu);
+
+/* extension: HOST state access: qp [N*36], qv [N*35], prev_act [N*29], steps [N], control
+ * tick (the RNG counter).  NULL pointers are skipped.  Synchronous. */
+void g1_env_get_state(void* h, float* qp, float* qv, float* pa, int* steps, unsigned long long* tick);
+void g1_env_set_state(void* h, const float* qp, const float* qv, const float* pa, const int* steps,
+                      unsigned long long tick);
+
+/* extension: contact-count histogram over substeps (ncon 0..8).  enable=1 (re)starts
+ * counting; out (HOST [9], may be NULL) receives the counts so far. */
+void g1_env_ncon_hist(void* h, int enable, unsigned long long* out);
+
+/* extension: per-state forward kinematics + generalized acceleration (the per-substep
+ * parity gate; semantics of the reference's src/test_envqacc.cu:29-51 with caller states).
+ * DEVICE pointers: qpos [n*36], qvel/tau/bdt [n*35] (tau, bdt may be NULL = 0) ->
+ * qacc, qacc_smooth, bias [n*35], f [n*32] contact impulses, ncon [n] (outputs may be NULL). */
+int g1_qacc_batch(int n, const float* qpos, const float* qvel, const float* tau, const float* bdt, int pgs_iters,
+                  float mu, float* qacc, float* qacc_smooth, float* bias, float* f, int* ncon);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* G1ENV_H */

@@ -1,0 +1,347 @@
+"""Benchmark of the fused G1 rollout (BASELINE.json metric: fused-rollout substeps/s per
+box, N=8192 worlds per GPU, H=32 control steps, S=10 substeps).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU)
+
+A step is one fused rollout (g1_rollout) of every world on this rank: N*H*S substeps.  The
+policy is the config-2 actor-critic (100 -> 256 -> 256 ELU -> 29 means + value, weights
+N(0, 1/fan_in), zero bias, log_std -0.5), observation stats mean 0 / var 1; data are
+synthetic (there is no dataset in this workload: the env generates its own states).
+Worlds are sharded across ranks (weak scaling); the rollout needs no communication, the
+timing is the max over ranks of CUDA-event time.
+
+Between timed steps the L2 is flushed (a 256 MiB write, outside the timed events).
+`--impl reference` times the reference implementation of the path on the host cores: the
+CPU oracle (oracle/g1_oracle.c, bit-identical to the reference's fp32 physics), OpenMP on
+all host threads, rank 0 only.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "g1.cu_b200"))
+
+N_PER_GPU, H, S, PGS = 8192, 32, 10, 8
+METRIC = "fused-rollout substeps/s per box at 1/2/4/8 B200 (N=8192/GPU, H=32); % roofline"
+CONFIG = {"workload": "config2: fused PPO rollout, N=8192 worlds/GPU, H=32, S=10, PGS 8, "
+                      "policy 100-256-256(ELU)-29+value fp32 random-init",
+          "worlds_per_gpu": N_PER_GPU, "horizon": H, "substeps": S, "pgs_iters": PGS,
+          "mlp": [100, 256, 256, 29], "activation": "elu", "l2": "flushed between timed steps (256 MiB write)"}
+
+# algorithmic FLOPs per world-substep by contact count (FK + env_qacc at PGS 8; mul and add
+# counted separately, FMA = 2), from the op-count of the reference physics at ncon 0/4/8
+# (35/72/122 kFLOP incl. FK); intermediate counts interpolated linearly between those.
+FLOP_NCON_ANCHORS = {0: 5673 + 29071, 4: 5673 + 65948, 8: 5673 + 116400}
+MLP_FLOP_PER_WORLD_STEP = 2 * (100 * 256 + 256 * 256 + 256 * 30)  # config-2 MLP incl. value head
+
+
+def flops_per_ncon():
+    a = FLOP_NCON_ANCHORS
+    out = []
+    for n in range(9):
+        lo, hi = (0, 4) if n <= 4 else (4, 8)
+        out.append(a[lo] + (a[hi] - a[lo]) * (n - lo) / (hi - lo))
+    return np.array(out)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p)), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx, self.rows, self.proc = gpu_index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def stop(self, t0=None, t1=None):
+        """Stop sampling; summarise the samples that arrived inside [t0, t1] (host time of the
+        timed region; the nearest sample if none did)."""
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        self.t.join(timeout=2)
+        ok = [(t, r) for t, r in self.rows if len(r) > 7 and r[1].replace(".", "").isdigit()]
+        sel = [r for t, r in ok if t0 is None or (t0 <= t <= t1 + 0.25)]
+        if not sel and ok:
+            sel = [min(ok, key=lambda x: abs(x[0] - (t0 or 0)))[1]]
+        sm = [float(r[1]) for r in sel]
+        mx = [float(r[2]) for r in sel if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in sel if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in sel for i in range(4) if r[4 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "reasons": reasons, "samples": len(sm)}
+
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        if args.impl == "reference":
+            dist.init_process_group("gloo")
+        else:
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if dist.get_backend() == "nccl" else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline(steps_sample=None, worlds_sample=None, target_s=10.0):
+    """The CPU oracle rollout on a bounded sample of the config-2 workload (worlds_sample
+    worlds x steps_sample control steps; by default sized from a short calibration run to
+    about target_s seconds), OpenMP over all host threads."""
+    if steps_sample is None or worlds_sample is None:
+        cal = cpu_baseline(2, 1024)
+        worlds_sample = 2048
+        steps_sample = int(np.clip(target_s * cal["value"] / (worlds_sample * S), 1, 512))
+    import torch  # noqa: F401  (policy init uses torch)
+    import g1env
+    from oracle.oracle import Oracle, OracleEnv
+    o = Oracle("f32")
+    cores = os.cpu_count() or 1
+    env = OracleEnv(o, worlds_sample, S, PGS, seed=1)
+    env.reset()
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (256, 256), "elu"), seed=0)
+    W = g1env.pack_weights(ac).detach().numpy()
+    mean, var = np.zeros(100, np.float32), np.ones(100, np.float32)
+    env.rollout(1, W, mean, var, act="elu")  # warm (thread pool)
+    t0 = time.perf_counter()
+    env.rollout(steps_sample, W, mean, var, act="elu")
+    dt = time.perf_counter() - t0
+    env.close()
+    sub = worlds_sample * steps_sample * S
+    return {"value": sub / dt, "unit": "substeps/s", "cores": cores, "kind": "port",
+            "sample": f"{worlds_sample} worlds x {steps_sample} control steps x {S} substeps "
+                      f"({sub} substeps, {dt:.1f} s) of the config-2 rollout, CPU oracle fp32 "
+                      f"(bit-identical to the reference's fp32 physics), OpenMP {cores} threads"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    t_all = []
+    for _ in range(args.warmup):
+        cpu_baseline(1, 64)
+    cal = cpu_baseline(2, 1024)
+    steps = int(np.clip(12.0 * cal["value"] / (2048 * S * max(args.steps, 1)), 1, 512))
+    for _ in range(args.steps):   # each step: a bounded sample of ~12/K s of CPU work
+        cb = cpu_baseline(steps, 2048)
+        t_all.append(cb["value"])
+    v = float(np.mean(t_all))
+    ms = 1e3 * N_PER_GPU * H * S / v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "substeps/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": CONFIG, "cpu_baseline": dict(cb, value=v),
+            "e2e": {"value": v, "unit": "substeps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def reference_kernel_time(N, mean, var, W, reps=2):
+    """The reference's own k_rollout (src/g1_env.cu compiled for sm_100a, oracle/_ref), same
+    workload, for the per-GPU speed-up target.  Returns ms per rollout or None."""
+    import ctypes
+    import torch
+    path = os.path.join(ROOT, "oracle", "_ref", "libg1env_ref.so")
+    if not os.path.exists(path):
+        return None
+    R = ctypes.CDLL(path)
+    R.g1_env_create.restype = ctypes.c_void_p
+    R.g1_env_create.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_ulong]
+    R.g1_env_reset.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    R.g1_rollout.argtypes = [ctypes.c_void_p, ctypes.c_int] + [ctypes.c_void_p] * 10
+    R.g1_env_destroy.argtypes = [ctypes.c_void_p]
+    h = R.g1_env_create(N, S, PGS, 1)
+    ob = np.zeros((N, 100), np.float32)
+    R.g1_env_reset(h, ob.ctypes.data_as(ctypes.c_void_p))
+    z = lambda *s: torch.zeros(*s, device="cuda")
+    bufs = [z(H, N, 100), z(H, N, 29), z(H, N), z(H, N), z(H, N), z(H, N), z(N)]
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    args = [vp(W), vp(mean), vp(var)] + [vp(b) for b in bufs]
+    R.g1_rollout(h, H, *args)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        R.g1_rollout(h, H, *args)
+    e1.record()
+    torch.cuda.synchronize()
+    R.g1_env_destroy(h)
+    return e0.elapsed_time(e1) / reps
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-ref-kernel", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    import torch
+    import g1env
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    N = N_PER_GPU
+    env = g1env.G1Env(N, S, PGS, seed=1, device=local, world0=rank * N)
+    env.set_policy((256, 256), "elu")
+    env.reset()
+    stream = torch.cuda.current_stream(dev)
+    env.set_stream(stream)
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (256, 256), "elu"), seed=0).to(dev)
+    W = g1env.pack_weights(ac).detach().contiguous()
+    mean = torch.zeros(100, device=dev)
+    var = torch.ones(100, device=dev)
+    z = lambda *s: torch.zeros(*s, device=dev)
+    bufs = [z(H, N, 100), z(H, N, 29), z(H, N), z(H, N), z(H, N), z(H, N), z(N)]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    for _ in range(args.warmup):
+        env.rollout(H, W, mean, var, *bufs)
+    torch.cuda.synchronize()
+    env.ncon_hist(True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    for _ in range(2):  # keep the GPU busy while the sampler spins up
+        env.rollout(H, W, mean, var, *bufs)
+    barrier(world)
+    torch.cuda.synchronize()
+    t_start = time.time()
+    times = []
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        env.rollout(H, W, mean, var, *bufs)
+        e1.record(stream)
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    t_end = time.time()
+    barrier(world)
+    ck = clocks.stop(t_start, t_end)
+    hist = env.ncon_hist(False).astype(np.float64)
+    ms_local = sum(a.elapsed_time(b) for a, b in times) / args.steps
+    ms = max_over_ranks(ms_local, world)
+    substeps = N * H * S
+    value = world * substeps / (ms * 1e-3)
+
+    # --- e2e through the public API with host buffers: pinned W/mean/var in, rewards/dones/
+    # bootstrap values out, every step
+    hW = W.cpu().pin_memory(); hm = mean.cpu().pin_memory(); hv = var.cpu().pin_memory()
+    dW, dm, dv = torch.empty_like(W), torch.empty_like(mean), torch.empty_like(var)
+    hR = torch.empty(H, N).pin_memory(); hD = torch.empty(H, N).pin_memory(); hVl = torch.empty(N).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize()
+    e_times = []
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dW.copy_(hW, non_blocking=True); dm.copy_(hm, non_blocking=True); dv.copy_(hv, non_blocking=True)
+        env.rollout(H, dW, dm, dv, *bufs)
+        hR.copy_(bufs[4], non_blocking=True); hD.copy_(bufs[5], non_blocking=True); hVl.copy_(bufs[6], non_blocking=True)
+        e1.record(stream)
+        e_times.append((e0, e1))
+    torch.cuda.synchronize()
+    ems = max_over_ranks(sum(a.elapsed_time(b) for a, b in e_times) / args.steps, world)
+    h2d = (W.numel() + 200) * 4
+    d2h = (2 * H * N + N) * 4
+
+    # --- roofline of the dominant kernel (k_g1): algorithmic FP32 FLOPs / kernel time
+    flop_sub = float((hist * flops_per_ncon()).sum() / max(hist.sum(), 1))
+    flops_launch = substeps * flop_sub + N * (H + 1) * MLP_FLOP_PER_WORLD_STEP
+    peaks, peak_src = load_peaks()
+    sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
+    clk = ck.get("sm_max_mhz") or peaks.get("sm_max_mhz", 1965.0)
+    fp32_peak = sm_count * 128 * 2 * clk * 1e6 / 1e12  # nominal FP32 FMA peak at max SM clock
+    achieved = flops_launch / (ms * 1e-3) / 1e12
+    ref_ms = None
+    if rank == 0 and not args.no_ref_kernel:
+        try:
+            ref_ms = reference_kernel_time(N, mean, var, W)
+        except Exception:  # the reference kernel is a comparison only
+            ref_ms = None
+    cpu = cpu_baseline() if (rank == 0 and world == 1) else None
+    env.close()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "substeps/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (env-generated states, random-init policy)",
+                "config": dict(CONFIG, parallelism=f"world shards x{world}, no rollout communication"),
+                "e2e": {"value": world * substeps / (ems * 1e-3), "unit": "substeps/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h},
+                "gpu_launches": 2 * args.steps,
+                "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+                             "frac": achieved / fp32_peak, "traffic": None,
+                             "peak_source": f"nominal FP32 FMA rate: {sm_count} SMs x 128 lanes x 2 x {clk:.0f} MHz "
+                                            f"(MEASURED_PEAKS.json has no FP32 figure; its hbm/bf16 peaks are {peak_src})",
+                             "flop_per_substep": flop_sub, "ncon_hist": hist.tolist()},
+                "clocks": ck,
+                "reference_kernel": None if ref_ms is None else {
+                    "ms_per_step": ref_ms, "value": substeps / (ref_ms * 1e-3), "unit": "substeps/s",
+                    "what": "reference k_rollout (src/g1_env.cu) built for sm_100a, same N/H/S, 1 GPU"}}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

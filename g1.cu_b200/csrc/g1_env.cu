@@ -830,19 +830,17 @@ int g1_qacc_batch(int n, const float* qpos, const float* qvel, const float* tau,
     return 0;
 }
 
-// extension (profiling builds only, -DG1_PROF): per-phase warp cycles since the last call.
-int g1_prof_read(unsigned long long* out) {
 #ifdef G1_PROF
+// profiling builds only (-DG1_PROF, not part of the shipped ABI): per-phase warp cycles
+// since the last call.
+int g1_prof_read(unsigned long long* out) {
     CKR(cudaDeviceSynchronize(), -1);
     CKR(cudaMemcpyFromSymbol(out, g_prof, sizeof(unsigned long long) * 16), -1);
     unsigned long long z[16] = {0};
     CKR(cudaMemcpyToSymbol(g_prof, z, sizeof z), -1);
     return 0;
-#else
-    (void)out;
-    return -1;
-#endif
 }
+#endif
 
 // g1_env.cu:365-382
 void g1_occupancy_report(void) {

@@ -1,0 +1,189 @@
+"""PPO on the fused GPU rollout, one process per GPU (the reference's scripts/ppo_fused.py
+training loop, ppo_fused.py:47-171, with world sharding across ranks).
+
+    python g1.cu_b200/ppo_fused.py [iters] [n_worlds_per_gpu] [--smoke] [--tag=name]
+    torchrun --nproc-per-node 8 g1.cu_b200/ppo_fused.py 1500 8192
+
+The rollout runs in the CUDA library (g1_rollout); torch does only the PPO update, reading
+the trajectory buffers in place.  With WORLD_SIZE > 1 each rank owns its own worlds (global
+world ids rank*N + i, so RNG streams are disjoint) and three things cross NCCL:
+  * the RunNorm moments of the raw observations (so every rank keeps the same frozen
+    normaliser, ppo_fused.py:104-106),
+  * the advantage moments for advantage normalisation (ppo_fused.py:119),
+  * the gradients, once per minibatch step (summed then divided by the world size).
+"""
+import os
+import sys
+import time
+
+import torch
+import torch.nn as nn
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from g1env import AC, G1Env, RunNorm, evaluate, pack_weights  # noqa: E402
+
+
+# ---------------------------------------------------------------- distributed helpers
+def _dist():
+    import torch.distributed as dist
+    return dist if dist.is_available() and dist.is_initialized() else None
+
+
+def global_moments(x):
+    """(mean, population var, count) of the rows of x over all ranks."""
+    dist = _dist()
+    n = torch.tensor([float(x.shape[0])], dtype=torch.float64, device=x.device)
+    s = x.double().sum(0)
+    ss = (x.double() ** 2).sum(0)
+    if dist is not None:
+        buf = torch.cat([n, s, ss])
+        dist.all_reduce(buf)
+        n, s, ss = buf[:1], buf[1:1 + s.numel()], buf[1 + s.numel():]
+    cnt = float(n.item())
+    mean = s / cnt
+    var = (ss / cnt - mean ** 2).clamp_min(0.0)
+    return mean.to(x.dtype), var.to(x.dtype), cnt
+
+
+def runnorm_update_global(norm, x):
+    """RunNorm.update (ppo.py:71-79) with the batch moments taken over all ranks."""
+    bm, bv, b = global_moments(x)
+    norm.update_from_moments(bm, bv, b)
+
+
+def normalize_advantages_global(adv):
+    """(adv - mean) / (std + 1e-8) with mean/std over all ranks (ppo_fused.py:119; torch.std
+    is the unbiased estimate)."""
+    m, v, n = global_moments(adv.reshape(-1, 1))
+    std = (v * n / max(n - 1.0, 1.0)).sqrt()
+    return (adv - m) / (std + 1e-8)
+
+
+def allreduce_grads(params):
+    """Average the gradients of `params` over ranks in one flat bucket."""
+    dist = _dist()
+    if dist is None:
+        return
+    grads = [p.grad for p in params if p.grad is not None]
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat)
+    flat /= dist.get_world_size()
+    off = 0
+    for g in grads:
+        n = g.numel()
+        g.copy_(flat[off:off + n].view_as(g))
+        off += n
+
+
+def broadcast_params(module):
+    dist = _dist()
+    if dist is None:
+        return
+    for p in module.parameters():
+        dist.broadcast(p.data, 0)
+
+
+def gae(R, V, D, Vlast, gamma=0.99, lam=0.95):
+    """GAE over the horizon (ppo_fused.py:108-116)."""
+    H = R.shape[0]
+    adv = torch.zeros_like(R)
+    g = torch.zeros_like(Vlast)
+    for t in reversed(range(H)):
+        nextv = Vlast if t == H - 1 else V[t + 1]
+        delta = R[t] + gamma * nextv * (1 - D[t]) - V[t]
+        g = delta + gamma * lam * (1 - D[t]) * g
+        adv[t] = g
+    return adv, adv + V
+
+
+def ppo_update(ac, opt, b_o, b_a, b_lp, b_adv, b_ret, epochs=5, mb=4, clip=0.2):
+    """The clipped PPO update of ppo_fused.py:121-140 (+ gradient all-reduce)."""
+    n = b_o.shape[0]
+    last = 0.0
+    params = list(ac.parameters())
+    for _ in range(epochs):
+        idx = torch.randperm(n, device=b_o.device)
+        for s in range(0, n, n // mb):
+            j = idx[s:s + n // mb]
+            mu, std, val = ac(b_o[j])
+            dist = torch.distributions.Normal(mu, std)
+            lp = dist.log_prob(b_a[j]).sum(-1)
+            ratio = (lp - b_lp[j]).exp()
+            s1 = ratio * b_adv[j]
+            s2 = torch.clamp(ratio, 1 - clip, 1 + clip) * b_adv[j]
+            pl = -torch.min(s1, s2).mean()
+            vl = (val - b_ret[j]).pow(2).mean()
+            ent = dist.entropy().sum(-1).mean()
+            loss = pl + 0.5 * vl - 0.01 * ent
+            opt.zero_grad()
+            loss.backward()
+            allreduce_grads(params)
+            nn.utils.clip_grad_norm_(params, 0.5)
+            opt.step()
+            last = float(loss.item())
+    return last
+
+
+def main():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    smoke = "--smoke" in sys.argv
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    iters = int(args[0]) if args else (3 if smoke else 1500)
+    N = int(args[1]) if len(args) > 1 else (256 if smoke else 8192)
+    H = 16 if smoke else 32
+    tag = next((a.split("=", 1)[1] for a in sys.argv if a.startswith("--tag=")), "fused")
+    out_dir = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "runs")
+    os.makedirs(out_dir, exist_ok=True)
+
+    env = G1Env(N, substeps=10, pgs_iters=8, seed=1, device=local, world0=rank * N)
+    O_dim, A_dim = env.obs_dim, env.act_dim
+    torch.manual_seed(0)
+    ac = AC(O_dim, A_dim).to(dev)
+    broadcast_params(ac)
+    norm = RunNorm(O_dim, dev)
+    opt = torch.optim.Adam(ac.parameters(), lr=3e-4)
+    z = lambda *s: torch.zeros(*s, device=dev)
+    O, A, LP, V, R, D, Vlast = z(H, N, O_dim), z(H, N, A_dim), z(H, N), z(H, N), z(H, N), z(H, N), z(N)
+    env.reset()
+    logf = open(os.path.join(out_dir, f"reward_curve_{tag}.csv"), "w") if rank == 0 else None
+    if logf:
+        logf.write("iter,mean_ep_rew_step,ret,loss,fwd_mean,ep_len,fall_rate,vx_mean,sps\n")
+    t0 = time.time()
+    for it in range(iters):
+        fmean, fvar = norm.mean.clone(), norm.var.clone()
+        W = pack_weights(ac).detach()
+        env.rollout(H, W, fmean, fvar, O, A, LP, V, R, D, Vlast)
+        with torch.no_grad():
+            nobs = torch.clamp((O - fmean) / torch.sqrt(fvar + 1e-8), -10.0, 10.0)
+            runnorm_update_global(norm, O.reshape(-1, O_dim))
+            adv, ret = gae(R, V, D, Vlast)
+            b_adv = normalize_advantages_global(adv.reshape(-1))
+        loss = ppo_update(ac, opt, nobs.reshape(-1, O_dim), A.reshape(-1, A_dim), LP.reshape(-1), b_adv, ret.reshape(-1))
+        sps = world * (it + 1) * H * N / (time.time() - t0)
+        ev = {"fwd_mean": float("nan"), "ep_len_mean": float("nan"), "fall_rate": float("nan"), "vx_mean": float("nan")}
+        if rank == 0 and ((it % 25 == 0) or it == iters - 1):
+            ev = evaluate(env, ac, norm, dev, steps=400 if not smoke else 20)
+            torch.save(dict(model=ac.state_dict(), obs_mean=norm.mean, obs_var=norm.var),
+                       os.path.join(out_dir, f"{tag}_last.pt"))
+        if rank == 0:
+            print(f"iter {it:4d} rew/step={R.mean().item():7.3f} loss={loss:7.3f} sps={sps:.2e}", flush=True)
+            logf.write(f"{it},{R.mean().item():.4f},{ret.mean().item():.4f},{loss:.4f},{ev['fwd_mean']:.4f},"
+                       f"{ev['ep_len_mean']:.2f},{ev['fall_rate']:.4f},{ev['vx_mean']:.4f},{sps:.3e}\n")
+            logf.flush()
+    env.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if smoke and rank == 0:
+        print("SMOKE OK: fused rollout + PPO update ran end-to-end.")
+
+
+if __name__ == "__main__":
+    main()

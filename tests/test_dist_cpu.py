@@ -1,0 +1,75 @@
+"""Multi-rank host logic of the PPO update on CPU (gloo, world size 2): the RunNorm moments,
+advantage normalisation and gradient averaging that cross NCCL on GPUs give the same result
+as one process holding all ranks' data."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import ppo_fused
+    from g1env import AC, RunNorm
+    g = torch.Generator().manual_seed(100 + rank)
+    x = torch.randn(50 + 30 * rank, 100, generator=g) * (1 + rank)
+    norm = RunNorm(100, "cpu")
+    ppo_fused.runnorm_update_global(norm, x)
+    adv = torch.randn(40 + 10 * rank, generator=g)
+    nadv = ppo_fused.normalize_advantages_global(adv)
+    torch.manual_seed(0)
+    ac = AC(100, 29)
+    ppo_fused.broadcast_params(ac)
+    out = ac(x[:8])[0].sum() * (rank + 1)
+    out.backward()
+    ppo_fused.allreduce_grads(list(ac.parameters()))
+    q.put((rank, x, norm.mean, norm.var, norm.count, adv, nadv, ac.mu.weight.grad.clone()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_distributed_stats_match_single_process():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = sorted([q.get(timeout=120) for _ in range(world)], key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "g1.cu_b200"))
+    from g1env import AC, RunNorm
+    xs = torch.cat([r[1] for r in res])
+    ref = RunNorm(100, "cpu")
+    ref.update(xs)
+    for r in res:
+        assert torch.allclose(r[2], ref.mean, atol=1e-5) and torch.allclose(r[3], ref.var, atol=1e-4)
+        assert abs(r[4] - ref.count) < 1e-6
+    adv = torch.cat([r[5] for r in res])
+    nadv = (adv - adv.mean()) / (adv.std() + 1e-8)
+    assert torch.allclose(torch.cat([r[6] for r in res]), nadv, atol=1e-5)
+    # gradient average: mean over ranks of (rank+1) * d sum(mu(x_rank[:8])) / dW
+    torch.manual_seed(0)
+    ac = AC(100, 29)
+    g_sum = 0
+    for r in res:
+        ac.zero_grad()
+        (ac(r[1][:8])[0].sum() * (r[0] + 1)).backward()
+        g_sum = g_sum + ac.mu.weight.grad.clone()
+    for r in res:
+        assert torch.allclose(r[7], g_sum / world, atol=1e-5)

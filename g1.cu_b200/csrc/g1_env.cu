@@ -37,7 +37,7 @@ using namespace g1;
 #define FINISH_BONUS 50.0f
 #define ACT_SCALE 0.5f
 
-#define NWARPS 14
+#define NWARPS 7
 #define NTHREADS (NWARPS * 32)
 #define MAX_WB 64          // worlds per CTA block, upper bound (MLP activations in smem)
 #define MAX_HIDDEN 4
@@ -125,58 +125,90 @@ __device__ __forceinline__ float obs_elem(int i, const float* qp, const float* q
 }
 
 // ------------------------------------------------------------------ policy phase
-// out[w][o] = act(b[o] + sum_i W[o][i] in[w][i]), i ascending (mlp_forward order,
-// g1_env.cu:230-237).  WT is [nin][nout] (coalesced across output lanes); a thread owns 2
-// outputs x 4 worlds so each weight pair is loaded once per 4 worlds.
+// out[w][o] = act(b[o] + sum_i W[o][i] in[w][i]), i ascending (the mlp_forward order,
+// g1_env.cu:230-237), for the nw worlds of the block.  WT is [nin][wstr] (W transposed);
+// weights are staged through shared memory in tiles of KT inputs x OC outputs (coalesced
+// loads, reused by every world of the block); a thread owns 2 outputs x 4 worlds of an
+// output chunk.  nin must be a multiple of 4 (inputs are read as float4).
+#define KT 32
+#define OC 64
 __device__ __noinline__ void cta_dense(const float* __restrict__ WT, int wstr, const float* __restrict__ bias, int nin, int nout,
-                          const float* in, int istr, float* out, int ostr, int nw, int act) {
-    const int nog = (nout + 1) >> 1, nwg = (nw + 3) >> 2;
-    for (int it = threadIdx.x; it < nog * nwg; it += blockDim.x) {
-        const int og = it % nog, wg = it / nog;
-        const int o0 = 2 * og, w0 = 4 * wg;
-        const bool has1 = o0 + 1 < nout;
-        float acc[4][2];
-        const float b0 = bias[o0], b1 = has1 ? bias[o0 + 1] : 0.f;
+                                       const float* in, int istr, float* out, int ostr, int nw, int act, float* wtile) {
+    const int nwg = (nw + 3) >> 2;
+    constexpr int NOG = OC / 2;
+    const int nitems = NOG * nwg;
+    constexpr int MAXIT = (NOG * (MAX_WB / 4) + NTHREADS - 1) / NTHREADS;
+    for (int oc0 = 0; oc0 < nout; oc0 += OC) {
+        float acc[MAXIT][4][2];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) { acc[k][0] = b0; acc[k][1] = b1; }
-        const float* xr[4];
+        for (int j = 0; j < MAXIT; ++j) {
+            const int it = threadIdx.x + j * NTHREADS;
+            const int o0 = oc0 + 2 * (it % NOG);
+            const float b0 = (it < nitems && o0 < nout) ? bias[o0] : 0.f;
+            const float b1 = (it < nitems && o0 + 1 < nout) ? bias[o0 + 1] : 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) xr[k] = in + (size_t)min(w0 + k, nw - 1) * istr;
-        for (int i = 0; i < nin; i += 4) {
-            float2 wv[4];
+            for (int k = 0; k < 4; ++k) { acc[j][k][0] = b0; acc[j][k][1] = b1; }
+        }
+        for (int k0 = 0; k0 < nin; k0 += KT) {
+            const int kt = min(KT, nin - k0);
+            __syncthreads();  // previous tile consumed
+            for (int e = threadIdx.x; e < KT * OC; e += NTHREADS) {
+                const int kk = e / OC, oo = e % OC;
+                wtile[e] = (kk < kt && oc0 + oo < nout) ? __ldg(WT + (size_t)(k0 + kk) * wstr + oc0 + oo) : 0.f;
+            }
+            __syncthreads();
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                wv[q] = (i + q < nin) ? (has1 ? __ldg(reinterpret_cast<const float2*>(WT + (size_t)(i + q) * wstr + o0))
-                                              : make_float2(__ldg(WT + (size_t)(i + q) * wstr + o0), 0.f))
-                                      : make_float2(0.f, 0.f);
+            for (int j = 0; j < MAXIT; ++j) {
+                const int it = threadIdx.x + j * NTHREADS;
+                if (it >= nitems) break;
+                const int og = it % NOG, w0 = 4 * (it / NOG);
+                const float* xr[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float4 x = *reinterpret_cast<const float4*>(xr[k] + i);
-                acc[k][0] += wv[0].x * x.x; acc[k][1] += wv[0].y * x.x;
-                if (i + 1 < nin) { acc[k][0] += wv[1].x * x.y; acc[k][1] += wv[1].y * x.y; }
-                if (i + 2 < nin) { acc[k][0] += wv[2].x * x.z; acc[k][1] += wv[2].y * x.z; }
-                if (i + 3 < nin) { acc[k][0] += wv[3].x * x.w; acc[k][1] += wv[3].y * x.w; }
+                for (int k = 0; k < 4; ++k) xr[k] = in + (size_t)min(w0 + k, nw - 1) * istr + k0;
+                const float* wt = wtile + 2 * og;
+                for (int kk = 0; kk < kt; kk += 4) {
+                    const float2 wa = *reinterpret_cast<const float2*>(wt + (kk + 0) * OC);
+                    const float2 wb = *reinterpret_cast<const float2*>(wt + (kk + 1) * OC);
+                    const float2 wc = *reinterpret_cast<const float2*>(wt + (kk + 2) * OC);
+                    const float2 wd = *reinterpret_cast<const float2*>(wt + (kk + 3) * OC);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float4 x = *reinterpret_cast<const float4*>(xr[k] + kk);
+                        acc[j][k][0] += wa.x * x.x; acc[j][k][1] += wa.y * x.x;
+                        acc[j][k][0] += wb.x * x.y; acc[j][k][1] += wb.y * x.y;
+                        acc[j][k][0] += wc.x * x.z; acc[j][k][1] += wc.y * x.z;
+                        acc[j][k][0] += wd.x * x.w; acc[j][k][1] += wd.y * x.w;
+                    }
+                }
             }
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            if (w0 + k >= nw) break;
+        for (int j = 0; j < MAXIT; ++j) {
+            const int it = threadIdx.x + j * NTHREADS;
+            if (it >= nitems) break;
+            const int o0 = oc0 + 2 * (it % NOG), w0 = 4 * (it / NOG);
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                if (j == 1 && !has1) break;
-                float s = acc[k][j];
-                if (act == 0) s = tanhf(s);
-                else if (act == 1) s = s > 0.f ? s : expm1f(s);
-                out[(size_t)(w0 + k) * ostr + o0 + j] = s;
+            for (int k = 0; k < 4; ++k) {
+                if (w0 + k >= nw) break;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    if (o0 + q >= nout) break;
+                    float v = acc[j][k][q];
+                    if (act == 0) v = tanhf(v);
+                    else if (act == 1) v = v > 0.f ? v : expm1f(v);
+                    out[(size_t)(w0 + k) * ostr + o0 + q] = v;
+                }
             }
         }
     }
+    __syncthreads();
 }
 
 // Policy phase for the CTA's world block: obs -> normalise -> MLP -> sample -> writes.
-// Leaves the block's actions in actb[w][29].  k_rollout body, g1_env.cu:296-318.
+// The block's actions go to A[t] (the physics phase reads them back from there).
+// k_rollout body, g1_env.cu:296-318.
 // final_value: only the value head is used (bootstrap Vlast, g1_env.cu:325-332).
-__device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, float* work, float* actb, int wbeg, int nbw, int t,
+__device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, float* work, int wbeg, int nbw, int t,
                              bool final_value) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* X = work;  // [nbw][XSTR]
@@ -185,6 +217,7 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
     const int hstr = ((maxw + 3) & ~3) + 4;
     float* H0 = X + MAX_WB * XSTR;
     float* H1 = H0 + MAX_WB * hstr;
+    float* WTILE = H1 + MAX_WB * hstr;  // [KT][OC]
     // observations (raw to O, normalised to X)
     for (int w = warp; w < nbw; w += NWARPS) {
         const int gw = wbeg + w;
@@ -209,14 +242,14 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
     for (int l = 0; l < P.nh; ++l) {
         const int no = P.hid[l];
         float* out = bufs[l & 1];
-        cta_dense(wp, no, wp + (size_t)nin * no, nin, no, in, istr, out, hstr, nbw, P.act);
+        cta_dense(wp, no, wp + (size_t)nin * no, nin, no, in, istr, out, hstr, nbw, P.act, WTILE);
         wp += (size_t)nin * no + no;
         in = out; nin = no; istr = hstr;
         __syncthreads();
     }
     // heads: 29 means + value (+2 pad) -> scratch row of 32 in X (X is dead now)
     float* HD = X;
-    cta_dense(wp, 32, wp + (size_t)nin * 32, nin, 30, in, istr, HD, 32, nbw, -1);
+    cta_dense(wp, 32, wp + (size_t)nin * 32, nin, 30, in, istr, HD, 32, nbw, -1, WTILE);
     const float* lsp = wp + (size_t)nin * 32 + 32;
     __syncthreads();
     // sampling: one thread per world, actions in index order (g1_env.cu:308-314)
@@ -236,7 +269,6 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
                 float ls = lsp[i];
                 float a = hd[i] + expf(ls) * nz;
                 lps += -0.5f * nz * nz - ls - 0.5f * LOG2PI;
-                actb[w * ACT_DIM + i] = a;
                 P.A[sb * ACT_DIM + i] = a;
             }
             P.LP[sb] = lps;
@@ -247,188 +279,216 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
 }
 
 // ------------------------------------------------------------------ physics phase
-// One control step of one world by one warp: PD targets, S substeps, reward, done,
-// auto-reset.  env_advance, g1_env.cu:118-212.
-__device__ void warp_control_step(const Params& P, const G1Tables& T, float* fr, int gw, const float* a, uint64_t tick,
-                                  float* r_out, int* d_out) {
-    using L = FrameLayout;
+// Named barrier that keeps the CTA's warps on the same substep (so they fetch the same code).
+__device__ __forceinline__ void substep_barrier() { asm volatile("bar.sync 1, %0;" ::"r"(NTHREADS) : "memory"); }
+
+// One control step of GW worlds (global ids wg0 .. wg0+nvalid-1; the remaining slots carry a
+// stand pose and are not written back) by one warp: PD targets, S substeps, reward, done,
+// auto-reset.  env_advance, g1_env.cu:118-212.  `acts`: actions of world wg0 (row-major
+// [.,29], null = zero action).
+__device__ void group_control_step(const Params& P, const G1Tables& T, float* grp, float* cw, int wg0, int nvalid,
+                                   const float* acts, uint64_t tick, float* r_out, float* d_out) {
     const int lane = threadIdx.x & 31;
-    float *qp = fr + L::QP, *qv = fr + L::QV, *tgt = fr + L::TGT, *tau = fr + L::TAU;
-    float* misc = fr + L::MISC;
     // load state
-    for (int i = lane; i < NQ; i += 32) qp[i] = P.qp[(size_t)gw * NQ + i];
-    for (int i = lane; i < NV; i += 32) qv[i] = P.qv[(size_t)gw * NV + i];
-    float pa_i = lane < ACT_DIM ? P.pa[(size_t)gw * NU + lane] : 0.f;
-    float a_i = lane < ACT_DIM ? a[lane] : 0.f;
-    if (lane < ACT_DIM) {
-        float t = T.target0[lane] + ACT_SCALE * a_i;
-        if (t < T.ctrl_lo[lane]) t = T.ctrl_lo[lane];
-        if (t > T.ctrl_hi[lane]) t = T.ctrl_hi[lane];
-        tgt[lane] = t;
+    for (int it = lane; it < GW * NQ; it += 32) {
+        const int w = it / NQ, i = it % NQ;
+        grp[w * WFLOATS + WL::QP + i] = w < nvalid ? P.qp[(size_t)(wg0 + w) * NQ + i] : T.qpos_stand[i];
     }
-    if (lane < 6) tau[lane] = 0.f;
-    float energy = 0.f, vx_sum = 0.f;
-    __syncwarp();
-    QaccOpts opt;
-    opt.pgs_iters = P.pgs; opt.mu = P.mu; opt.bdt = T.bdt;
-    for (int s = 0; s < P.S; ++s) {
-        if (P.lockstep) asm volatile("bar.sync 1, %0;" ::"r"(NTHREADS) : "memory");
-#ifdef G1_PROF
-        long long _pt = clock64();
-#endif
-        float e = 0.f;
-        if (lane < ACT_DIM) {
-            int d = T.act_dof[lane];
-            float pdt = T.kp[lane] * (tgt[lane] - qp[T.act_qadr[lane]]) - T.kd[lane] * qv[d];
-            if (pdt < T.frc_lo[lane]) pdt = T.frc_lo[lane];
-            else if (pdt > T.frc_hi[lane]) pdt = T.frc_hi[lane];
-            tau[d] = pdt;
-            e = fabsf(pdt * qv[d]);
-        }
-        // energy accumulates actuator by actuator in index order (g1_env.cu:151)
+    for (int it = lane; it < GW * 36; it += 32) {
+        const int w = it / 36, i = it % 36;
+        float* fr = grp + w * WFLOATS;
+        fr[WL::QV + i] = (w < nvalid && i < NV) ? P.qv[(size_t)(wg0 + w) * NV + i] : 0.f;
+        fr[WL::TAU + i] = 0.f;
+    }
+    for (int it = lane; it < GW * ACT_DIM; it += 32) {
+        const int w = it / ACT_DIM, i = it % ACT_DIM;
+        const float a = (acts && w < nvalid) ? acts[(size_t)w * ACT_DIM + i] : 0.f;
+        float t = T.target0[i] + ACT_SCALE * a;
+        if (t < T.ctrl_lo[i]) t = T.ctrl_lo[i];
+        if (t > T.ctrl_hi[i]) t = T.ctrl_hi[i];
+        grp[w * WFLOATS + WL::TGT + i] = t;
+    }
+    float energy = 0.f, vx_sum = 0.f;  // lane w < GW: world w
+    const float* bdt_all[GW];
 #pragma unroll
-        for (int i = 0; i < ACT_DIM; ++i) energy += __shfl_sync(FULLMASK, e, i);
+    for (int w = 0; w < GW; ++w) bdt_all[w] = T.bdt;
+    QaccOpts opt;
+    opt.pgs_iters = P.pgs; opt.mu = P.mu; opt.bdt = bdt_all;
+    __syncwarp();
+    for (int s = 0; s < P.S; ++s) {
+        if (P.lockstep) substep_barrier();
+        PROF_BEGIN();
+        // PD torque, clamped to the actuator range; |tau qd| kept per actuator for the energy
+        for (int it = lane; it < GW * ACT_DIM; it += 32) {
+            const int w = it / ACT_DIM, i = it % ACT_DIM;
+            float* fr = grp + w * WFLOATS;
+            const int d = T.act_dof[i];
+            float pdt = T.kp[i] * (fr[WL::TGT + i] - fr[WL::QP + T.act_qadr[i]]) - T.kd[i] * fr[WL::QV + d];
+            if (pdt < T.frc_lo[i]) pdt = T.frc_lo[i];
+            else if (pdt > T.frc_hi[i]) pdt = T.frc_hi[i];
+            fr[WL::TAU + d] = pdt;
+            fr[WL::CON + i] = fabsf(pdt * fr[WL::QV + d]);
+        }
+        __syncwarp();
+        if (lane < GW) {  // energy accumulates actuator by actuator in index order (g1_env.cu:151)
+            const float* e = grp + lane * WFLOATS + WL::CON;
+            for (int i = 0; i < ACT_DIM; ++i) energy += e[i];
+        }
         __syncwarp();
         PROF_MARK(P_STEP);
-        int ncon = warp_qacc(fr, T, lane, opt);
-        if (P.ncon_hist && lane == 0) atomicAdd(&P.ncon_hist[ncon], 1);
+        int ncon[GW];
+        group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon);
+        if (P.ncon_hist && lane == 0)
+            for (int w = 0; w < nvalid; ++w) atomicAdd(&P.ncon_hist[ncon[w]], 1);
         {
             PROF_BEGIN();
-            warp_integrate(fr, T, lane, true);
-            vx_sum += qv[0];
-            PROF_MARK(P_STEP);
+            group_integrate(grp, T, lane, true);
+            if (lane < GW) vx_sum += grp[lane * WFLOATS + WL::QV];
+            PROF_MARK(P_INTEG);
         }
     }
-    // reward / termination (g1_env.cu:164-197)
-    float vx = vx_sum / (float)P.S, height = qp[2];
-    float m[9];
-    qmat(ld4(qp + 3), m);
-    float up = m[8];
-    int alive = (height < 0.45f || up < 0.5f) ? 0 : 1;
-    float upc = up < 0.f ? 0.f : (up > 1.f ? 1.f : up);
-    float vxc = vx > CMD_VX ? CMD_VX : vx;
-    if (vxc < 0.f) vxc = 0.f;
-    float r_vel = 1.0f * vxc * upc;
-    float r_lat = -0.2f * fabsf(qv[1]) - 0.05f * fabsf(qv[5]);
-    float r_up = 0.3f * upc;
-    float r_h = -0.5f * fabsf(height - 0.78f);
-    float dai = a_i - pa_i, pterm = dai * dai;
-    float act_pen = 0.f;
-#pragma unroll
-    for (int i = 0; i < ACT_DIM; ++i) act_pen += __shfl_sync(FULLMASK, pterm, i);
-    if (act_pen > 10.f) act_pen = 10.f;
-    float r = alive ? 1.0f + r_vel + r_lat + r_up + r_h - 0.005f * act_pen - 1e-4f * energy : -5.0f;
-    int step = P.steps[gw] + 1;
-    int won = (alive && qp[0] >= X_FIN);
-    if (won) r += FINISH_BONUS;
-    int d_flag = (!alive || won || step >= 1000) ? 1 : 0;
-    __syncwarp();
-    float pa_new = a_i;
-    if (d_flag) {  // auto-reset (g1_env.cu:202-210)
-        for (int i = lane; i < NQ; i += 32) qp[i] = T.qpos_stand[i];
-        __syncwarp();
-        if (lane < ACT_DIM) {
-            uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)gw, tick, RNG_AUTORESET, (uint32_t)lane);
-            qp[T.act_qadr[lane]] += 0.05f * (u01_open(rb.x) * 2.f - 1.f);
+    // reward / termination per world (g1_env.cu:164-197), lane w
+    int d_flag = 0;
+    if (lane < nvalid) {
+        const int w = lane, gw = wg0 + w;
+        const float* fr = grp + w * WFLOATS;
+        const float* qp = fr + WL::QP;
+        const float* qv = fr + WL::QV;
+        const float vx = vx_sum / (float)P.S, height = qp[2];
+        float m[9];
+        qmat(ld4(qp + 3), m);
+        const float up = m[8];
+        const int alive = (height < 0.45f || up < 0.5f) ? 0 : 1;
+        const float upc = up < 0.f ? 0.f : (up > 1.f ? 1.f : up);
+        float vxc = vx > CMD_VX ? CMD_VX : vx;
+        if (vxc < 0.f) vxc = 0.f;
+        const float r_vel = 1.0f * vxc * upc;
+        const float r_lat = -0.2f * fabsf(qv[1]) - 0.05f * fabsf(qv[5]);
+        const float r_up = 0.3f * upc;
+        const float r_h = -0.5f * fabsf(height - 0.78f);
+        float act_pen = 0.f;
+        for (int i = 0; i < ACT_DIM; ++i) {
+            const float da = (acts ? acts[(size_t)w * ACT_DIM + i] : 0.f) - P.pa[(size_t)gw * NU + i];
+            act_pen += da * da;
         }
-        for (int i = lane; i < NV; i += 32) qv[i] = 0.f;
-        pa_new = 0.f;
-        step = 0;
+        if (act_pen > 10.f) act_pen = 10.f;
+        float r = alive ? 1.0f + r_vel + r_lat + r_up + r_h - 0.005f * act_pen - 1e-4f * energy : -5.0f;
+        const int step = P.steps[gw] + 1;
+        const int won = (alive && qp[0] >= X_FIN);
+        if (won) r += FINISH_BONUS;
+        d_flag = (!alive || won || step >= 1000) ? 1 : 0;
+        P.steps[gw] = d_flag ? 0 : step;
+        r_out[w] = r;
+        d_out[w] = (float)d_flag;
+    }
+    unsigned dmask = __ballot_sync(FULLMASK, d_flag != 0);
+    __syncwarp();
+    // auto-reset (g1_env.cu:202-210), store state and previous action
+    for (int it = lane; it < GW * NQ; it += 32) {
+        const int w = it / NQ, i = it % NQ;
+        if ((dmask >> w) & 1u) grp[w * WFLOATS + WL::QP + i] = T.qpos_stand[i];
     }
     __syncwarp();
-    for (int i = lane; i < NQ; i += 32) P.qp[(size_t)gw * NQ + i] = qp[i];
-    for (int i = lane; i < NV; i += 32) P.qv[(size_t)gw * NV + i] = qv[i];
-    if (lane < ACT_DIM) P.pa[(size_t)gw * NU + lane] = pa_new;
-    if (lane == 0) P.steps[gw] = step;
-    (void)misc;
-    *r_out = r;
-    *d_out = d_flag;
+    for (int it = lane; it < GW * ACT_DIM; it += 32) {
+        const int w = it / ACT_DIM, i = it % ACT_DIM;
+        if (w >= nvalid) continue;
+        const int gw = wg0 + w;
+        if ((dmask >> w) & 1u) {
+            const uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)gw, tick, RNG_AUTORESET, (uint32_t)i);
+            grp[w * WFLOATS + WL::QP + T.act_qadr[i]] += 0.05f * (u01_open(rb.x) * 2.f - 1.f);
+            P.pa[(size_t)gw * NU + i] = 0.f;
+        } else {
+            P.pa[(size_t)gw * NU + i] = acts ? acts[(size_t)w * ACT_DIM + i] : 0.f;
+        }
+    }
+    __syncwarp();
+    for (int it = lane; it < GW * NQ; it += 32) {
+        const int w = it / NQ, i = it % NQ;
+        if (w < nvalid) P.qp[(size_t)(wg0 + w) * NQ + i] = grp[w * WFLOATS + WL::QP + i];
+    }
+    for (int it = lane; it < GW * NV; it += 32) {
+        const int w = it / NV, i = it % NV;
+        if (w < nvalid) P.qv[(size_t)(wg0 + w) * NV + i] = ((dmask >> w) & 1u) ? 0.f : grp[w * WFLOATS + WL::QV + i];
+    }
+    __syncwarp();
 }
 
 // ------------------------------------------------------------------ the kernel
 struct SmemPlan {
-    int tab_floats, frame_floats, actb_floats, total_bytes;
+    int tab_floats, group_floats, total_bytes;
 };
 __host__ __device__ inline SmemPlan smem_plan() {
     SmemPlan p;
     p.tab_floats = ((int)((sizeof(G1Tables) + 15) / 16)) * 4;
-    p.frame_floats = NWARPS * FRAME_FLOATS;
-    p.actb_floats = MAX_WB * ACT_DIM + 4;
-    p.total_bytes = (p.tab_floats + p.frame_floats + p.actb_floats) * 4;
+    p.group_floats = GROUP_FLOATS + GW * 36;  // + per-world damping rows (k_qacc)
+    p.total_bytes = (p.tab_floats + NWARPS * p.group_floats + 4) * 4;
     return p;
+}
+static_assert(MAX_WB * XSTR + 2 * MAX_WB * 260 + KT * OC <= NWARPS * GROUP_FLOATS, "MLP activations must fit in the frames");
+
+__device__ __forceinline__ void load_tables(float* smem) {
+    const int4* src = reinterpret_cast<const int4*>(&c_tab);
+    int4* dst = reinterpret_cast<int4*>(smem);
+    for (int i = threadIdx.x; i < (int)(sizeof(G1Tables) / 16); i += blockDim.x) dst[i] = src[i];
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     const SmemPlan plan = smem_plan();
-    {  // model tables -> shared memory
-        const int4* src = reinterpret_cast<const int4*>(&c_tab);
-        int4* dst = reinterpret_cast<int4*>(smem);
-        for (int i = threadIdx.x; i < (int)(sizeof(G1Tables) / 16); i += blockDim.x) dst[i] = src[i];
-    }
+    load_tables(smem);
     const G1Tables& T = *reinterpret_cast<const G1Tables*>(smem);
     float* frames = smem + plan.tab_floats;
-    float* actb = frames + plan.frame_floats;
-    int* qctr = reinterpret_cast<int*>(actb + MAX_WB * ACT_DIM);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* fr = frames + warp * FRAME_FLOATS;
+    float* grp = frames + warp * plan.group_floats;
+    float* cw = grp + GW * WFLOATS;
     __syncthreads();
 
     const int wbeg = blockIdx.x * P.wb;
     const int nbw = min(P.wb, P.N - wbeg);
     if (nbw <= 0) return;
     const int nsteps = P.mode == MODE_ROLLOUT ? P.H : (P.mode == MODE_PHYS ? P.K : 1);
+    const int nrounds = (nbw + GW * NWARPS - 1) / (GW * NWARPS);
     for (int t = 0; t < nsteps; ++t) {
         const uint64_t tick = P.tick0 + (uint64_t)t;
-        PROF_BEGIN();
         if (P.mode == MODE_ROLLOUT) {
-            policy_phase(P, T, frames, actb, wbeg, nbw, t, false);
+            PROF_BEGIN();
+            policy_phase(P, T, frames, wbeg, nbw, t, false);
             PROF_MARK(P_POLICY);
-        } else {
-            for (int i = threadIdx.x; i < nbw * ACT_DIM; i += blockDim.x)
-                actb[i] = P.mode == MODE_STEP ? P.act_in[(size_t)wbeg * ACT_DIM + i] : 0.f;
         }
-        if (threadIdx.x == 0) *qctr = 0;
         __syncthreads();
-        // physics: warps pull worlds from the block queue (or, in lockstep mode, take worlds
-        // warp, warp+NWARPS, ... and idle through the substep barriers when out of worlds)
-        for (int round = 0;; ++round) {
-            int w = 0;
-            if (P.lockstep) {
-                if (round * NWARPS >= nbw) break;
-                w = warp + round * NWARPS;
-                if (w >= nbw) {
-                    for (int s = 0; s < P.S; ++s) asm volatile("bar.sync 1, %0;" ::"r"(NTHREADS) : "memory");
-                    continue;
-                }
-            } else {
-                if (lane == 0) w = atomicAdd(qctr, 1);
-                w = __shfl_sync(FULLMASK, w, 0);
-                if (w >= nbw) break;
+        // physics: warp takes world groups warp, warp + NWARPS, ... of the block; a warp with no
+        // group in a round still passes the substep barriers
+        for (int round = 0; round < nrounds; ++round) {
+            const int w0 = (warp + round * NWARPS) * GW;
+            const int nvalid = max(0, min(GW, nbw - w0));
+            if (nvalid == 0) {
+                if (P.lockstep)
+                    for (int s = 0; s < P.S; ++s) substep_barrier();
+                continue;
             }
-            const int gw = wbeg + w;
-            float r;
-            int d;
-            warp_control_step(P, T, fr, gw, actb + w * ACT_DIM, tick, &r, &d);
-            if (lane == 0) {
+            const int wg0 = wbeg + w0;
+            const float* acts = P.mode == MODE_ROLLOUT ? P.A + ((size_t)t * P.N + wg0) * ACT_DIM
+                              : (P.mode == MODE_STEP ? P.act_in + (size_t)wg0 * ACT_DIM : nullptr);
+            float r[GW], d[GW];
+            group_control_step(P, T, grp, cw, wg0, nvalid, acts, tick, r, d);
+            if (lane < nvalid) {
+                const int gw = wg0 + lane;
                 if (P.mode == MODE_ROLLOUT) {
-                    P.R[(size_t)t * P.N + gw] = r;
-                    P.D[(size_t)t * P.N + gw] = (float)d;
+                    P.R[(size_t)t * P.N + gw] = r[lane];
+                    P.D[(size_t)t * P.N + gw] = d[lane];
                 } else if (P.mode == MODE_STEP) {
-                    P.rew_out[gw] = r;
-                    P.done_out[gw] = (float)d;
+                    P.rew_out[gw] = r[lane];
+                    P.done_out[gw] = d[lane];
                 }
             }
             if (P.mode == MODE_STEP) {  // k_step's obs after the step (g1_env.cu:265-266)
-                using L = FrameLayout;
                 __syncwarp();
-                const float* qp = P.qp + (size_t)gw * NQ;  // written back by this warp
-                const float* qv = P.qv + (size_t)gw * NV;
-                const float* pa = P.pa + (size_t)gw * NU;
-                __syncwarp();
-                for (int i = lane; i < OBS_DIM; i += 32) P.obs_out[(size_t)gw * OBS_DIM + i] = obs_elem(i, qp, qv, pa, T);
-                (void)sizeof(L);
+                for (int it = lane; it < nvalid * OBS_DIM; it += 32) {
+                    const int w = it / OBS_DIM, i = it % OBS_DIM, gw = wg0 + w;
+                    P.obs_out[(size_t)gw * OBS_DIM + i] =
+                        obs_elem(i, P.qp + (size_t)gw * NQ, P.qv + (size_t)gw * NV, P.pa + (size_t)gw * NU, T);
+                }
             }
             __syncwarp();
         }
@@ -438,46 +498,59 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
             PROF_MARK(P_WAIT);
         }
     }
-    if (P.mode == MODE_ROLLOUT) policy_phase(P, T, frames, actb, wbeg, nbw, 0, true);
+    if (P.mode == MODE_ROLLOUT) policy_phase(P, T, frames, wbeg, nbw, 0, true);
 }
 
-// Per-state FK + generalized acceleration (the reference's test_envqacc.cu harness
-// semantics, with caller states): one warp per state.
+// Per-state FK + generalised acceleration (the reference's test_envqacc.cu harness
+// semantics, with caller states): a warp takes GW states at a time.
 __global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, const float* qvel, const float* tau,
                                                       const float* bdt, int pgs, float mu, float* qacc_out,
                                                       float* qacc_s_out, float* bias_out, float* f_out, int* ncon_out) {
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     const SmemPlan plan = smem_plan();
-    {
-        const int4* src = reinterpret_cast<const int4*>(&c_tab);
-        int4* dst = reinterpret_cast<int4*>(smem);
-        for (int i = threadIdx.x; i < (int)(sizeof(G1Tables) / 16); i += blockDim.x) dst[i] = src[i];
-    }
+    load_tables(smem);
     __syncthreads();
     const G1Tables& T = *reinterpret_cast<const G1Tables*>(smem);
-    using L = FrameLayout;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* fr = smem + plan.tab_floats + warp * FRAME_FLOATS;
-    float* bd = smem + plan.tab_floats + plan.frame_floats + warp * 36;  // per-warp damping
-    for (int w = blockIdx.x * NWARPS + warp; w < n; w += gridDim.x * NWARPS) {
-        for (int i = lane; i < NQ; i += 32) fr[L::QP + i] = qpos[(size_t)w * NQ + i];
-        for (int i = lane; i < NV; i += 32) {
-            fr[L::QV + i] = qvel[(size_t)w * NV + i];
-            fr[L::TAU + i] = tau ? tau[(size_t)w * NV + i] : 0.f;
-            bd[i] = bdt ? bdt[(size_t)w * NV + i] : 0.f;
+    float* grp = smem + plan.tab_floats + warp * plan.group_floats;
+    float* cw = grp + GW * WFLOATS;
+    float* bd = cw + CFLOATS;  // [GW][36]
+    for (int s0 = (blockIdx.x * NWARPS + warp) * GW; s0 < n; s0 += gridDim.x * NWARPS * GW) {
+        const int nvalid = min(GW, n - s0);
+        for (int it = lane; it < GW * 36; it += 32) {
+            const int w = it / 36, i = it % 36;
+            float* fr = grp + w * WFLOATS;
+            const bool ok = w < nvalid;
+            const size_t st = (size_t)(s0 + (ok ? w : 0));
+            fr[WL::QP + i] = ok && i < NQ ? qpos[st * NQ + i] : (i < NQ ? T.qpos_stand[i] : 0.f);
+            fr[WL::QV + i] = ok && i < NV ? qvel[st * NV + i] : 0.f;
+            fr[WL::TAU + i] = ok && i < NV && tau ? tau[st * NV + i] : 0.f;
+            bd[w * 36 + i] = ok && i < NV && bdt ? bdt[st * NV + i] : 0.f;
         }
         __syncwarp();
-        QaccOpts opt;
-        opt.pgs_iters = pgs; opt.mu = mu; opt.bdt = bd;
-        int ncon = warp_qacc(fr, T, lane, opt);
-        for (int i = lane; i < NV; i += 32) {
-            if (qacc_out) qacc_out[(size_t)w * NV + i] = fr[L::QACC + i];
-            if (qacc_s_out) qacc_s_out[(size_t)w * NV + i] = fr[L::MM + i];
-            if (bias_out) bias_out[(size_t)w * NV + i] = fr[L::BIAS + i];
+        const float* bdt_w[GW];
+        float* bias_w[GW];
+        float* f_w[GW];
+        float* qs_w[GW];
+#pragma unroll
+        for (int w = 0; w < GW; ++w) {
+            const bool ok = w < nvalid;
+            bdt_w[w] = bd + w * 36;
+            bias_w[w] = (ok && bias_out) ? bias_out + (size_t)(s0 + w) * NV : nullptr;
+            f_w[w] = (ok && f_out) ? f_out + (size_t)(s0 + w) * MAXEFC : nullptr;
+            qs_w[w] = (ok && qacc_s_out) ? qacc_s_out + (size_t)(s0 + w) * NV : nullptr;
         }
-        if (f_out) f_out[(size_t)w * MAXEFC + lane] = lane < 4 * ncon ? fr[L::FF + lane] : 0.f;
-        if (ncon_out && lane == 0) ncon_out[w] = ncon;
+        QaccOpts opt;
+        opt.pgs_iters = pgs; opt.mu = mu; opt.bdt = bdt_w;
+        int ncon[GW];
+        group_qacc(grp, cw, T, lane, opt, bias_w, f_w, ncon, qs_w);
+        for (int it = lane; it < nvalid * NV; it += 32) {
+            const int w = it / NV, i = it % NV;
+            const float* fr = grp + w * WFLOATS;
+            if (qacc_out) qacc_out[(size_t)(s0 + w) * NV + i] = fr[WL::QACC + i];
+        }
+        if (ncon_out && lane < nvalid) ncon_out[s0 + lane] = ncon[lane];
         __syncwarp();
     }
 }
@@ -566,6 +639,7 @@ static int upload_tables(int dev) {
         SmemPlan p = smem_plan();
         if (cudaFuncSetAttribute(k_g1, cudaFuncAttributeMaxDynamicSharedMemorySize, p.total_bytes) != cudaSuccess) rc = -2;
         if (cudaFuncSetAttribute(k_qacc, cudaFuncAttributeMaxDynamicSharedMemorySize, p.total_bytes) != cudaSuccess) rc = -3;
+        if (T.nchain > CPW) rc = -4;  // the chain-lane mapping holds at most CPW chains
     });
     return rc;
 }
@@ -671,12 +745,12 @@ int g1_env_set_policy(void* h, int nh, const int* hidden, int activation) {
     EnvState* E = (EnvState*)h;
     if (nh < 1 || nh > MAX_HIDDEN || activation < 0 || activation > 1) { set_error(-22, "g1_env_set_policy", "invalid"); return -22; }
     for (int i = 0; i < nh; ++i)
-        if (hidden[i] < 1 || hidden[i] > 1024 || (hidden[i] & 1)) { set_error(-22, "g1_env_set_policy", "bad width"); return -22; }
+        if (hidden[i] < 4 || hidden[i] > 1024 || (hidden[i] & 3)) { set_error(-22, "g1_env_set_policy", "bad width"); return -22; }
     // MLP activations for MAX_WB worlds must fit in the physics frames it aliases
     int maxw = 0;
     for (int i = 0; i < nh; ++i) maxw = hidden[i] > maxw ? hidden[i] : maxw;
-    size_t need = (size_t)MAX_WB * XSTR + 2 * (size_t)MAX_WB * (((maxw + 3) & ~3) + 4);
-    if (need > (size_t)NWARPS * FRAME_FLOATS) { set_error(-22, "g1_env_set_policy", "hidden width too large for this build"); return -22; }
+    size_t need = (size_t)MAX_WB * XSTR + 2 * (size_t)MAX_WB * (((maxw + 3) & ~3) + 4) + KT * OC;
+    if (need > (size_t)NWARPS * GROUP_FLOATS) { set_error(-22, "g1_env_set_policy", "hidden width too large for this build"); return -22; }
     E->nh = nh; E->act = activation;
     for (int i = 0; i < MAX_HIDDEN; ++i) E->hid[i] = i < nh ? hidden[i] : 0;
     return 0;

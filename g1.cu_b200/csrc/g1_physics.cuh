@@ -1,16 +1,15 @@
-// g1_physics.cuh -- per-substep G1 dynamics for ONE world, executed by ONE warp.
+// g1_physics.cuh -- per-substep G1 dynamics, GW worlds per warp, frames in shared memory.
 //
 // The reference runs a world per thread and keeps its ~25 KB working set in local memory
-// (g1_env.cu:245, "255 regs, ~25-31 KB local frame").  Here a warp owns a world and its
-// frame lives in shared memory; lanes split every step of the algorithm over the
-// independent items it offers:
-//   forward kinematics / RNE        one lane per body of a tree level  (root->leaf)
-//   motion axes, body inertias      one lane per dof / per body
-//   articulated-inertia factor      one lane per body of a level       (leaf->root, pull)
-//   M^-1 back-solves                one lane per right-hand side: the smooth solve and the
-//                                   3*ncon contact basis columns run together (25 lanes)
-//   Gram / Delassus blocks          one lane per (contact pair, basis entry)
-//   PGS                             one lane per constraint row, rows swept in order
+// (g1_env.cu:245, "255 regs, ~25-31 KB local frame").  Here a warp advances GW = 4 worlds
+// together with their frames in shared memory, and splits the work over independent items:
+//   tree sweeps (FK, RNE, factor, smooth solve)  one lane per (world, chain of the tree)
+//   contact detection                            one lane per (world, foot sphere)
+//   contact solve, one world at a time:
+//     M^-1 of the contact basis                  one lane per basis column (<= 24)
+//     Gram / Delassus blocks                     one lane per (contact pair, entry)
+//     PGS                                        one lane per constraint row, rows in order
+//   integration                                  one lane per (world, dof / joint)
 // Within each item the arithmetic follows the reference's order (citations per function),
 // so results agree with it to fp32 rounding.
 #pragma once
@@ -22,57 +21,6 @@ namespace g1 {
 
 constexpr int NB = G1_NB, NV = G1_NV_, NQ = G1_NQ_, NJ = G1_NJ, NU = G1_NU_, NFOOT = G1_NFOOT_;
 constexpr int MAXCON = G1_MAXCON, MAXEFC = G1_MAXEFC, CDS = G1_CDS, NRHS = G1_NRHS;
-constexpr int ASTR = 33;   // row stride of the Delassus matrix in shared memory
-constexpr int MSTR = 35;   // row stride of the back-solve buffer (35 is odd: conflict-free per lane row)
-
-// compile-time tree for the fully unrolled per-lane back-solve
-__device__ constexpr int kParent[NB] = {G1M_BODY_PARENT_LIST};
-__device__ constexpr int kDofAdr[NB] = {G1M_BODY_DOFADR_LIST};
-
-// ------------------------------------------------------------------ frame layout
-// Offsets (in floats) inside one warp's shared-memory frame.
-struct FrameLayout {
-    enum : int {
-        QP = 0,                    // qpos[36]
-        QV = QP + 36,              // qvel[35] (+1)
-        TGT = QV + 36,             // PD targets [29] (+3)
-        TAU = TGT + 32,            // generalized force [35] (+1)
-        QACC = TAU + 36,           // result qacc [35] (+1)
-        MISC = QACC + 36,          // 16 scalars
-        S = MISC + 16,             // motion axes [35*6]
-        FU = S + 210,              // factor: U [31*6]
-        FINVD = FU + 186,          // factor: 1/D [31] (+1)
-        FU6 = FINVD + 32,          // base: U6 [36]
-        FL6 = FU6 + 36,            // base: Dm, then its Cholesky factor [36]
-        BIAS = FL6 + 36,           // qfrc_bias [35] (+1)
-        CON = BIAS + 36,           // contacts: sphere(int) [8], pt [8*3], pen [8]
-        EB = CON + 40,             // basis rows [8][3][12]
-        BB = EB + 288,             // (spare) [24]
-        RR = BB + 24,              // R [32]
-        AREF = RR + 32,            // (spare) [32]
-        BV = AREF + 32,            // b [32]
-        FF = BV + 32,              // impulses f [32]
-        MM = FF + 32,              // [25][35]: row 0 qacc_smooth, rows 1+3c+a contact basis solves
-        UNION = MM + NRHS * MSTR,  // tree sweep scratch | Gram + Delassus matrix
-        // union part 1: tree sweeps (dead once the contact basis is built)
-        XPOS = UNION,              // body positions [31*3] (+3)
-        XQUAT = XPOS + 96,         // body orientations [31*4]
-        IAB = XQUAT + 124,         // per body: own articulated inertia, then its contribution [31*21]
-        FOWN = IAB + NB * 21,      // per body: own force, then subtree force [31*6]
-        PAC = FOWN + NB * 6,       // per body: articulated bias-force contribution [31*6]
-        UB = PAC + NB * 6,         // per body: u_b = x_d - S_d.pA_b [31] (+1)
-        BST = UB + 32,             // branch hand-off slots: pos,quat,w,v,aw,av (19) + a (6) -> 26 each
-        A1 = BST + G1_MAXBRANCH * 26,  // base spatial acceleration [6] (+2)
-        U1_END = A1 + 8,
-        // union part 2
-        GRAM = UNION,              // [36 pairs][9]
-        AMAT = GRAM + 324,         // [32][33]
-        U2_END = AMAT + MAXEFC * ASTR,
-        SIZE = (U1_END > U2_END ? U1_END : U2_END)
-    };
-};
-
-constexpr int FRAME_FLOATS = (FrameLayout::SIZE + 3) & ~3;
 
 // ------------------------------------------------------------------ small algebra
 struct V3 { float x, y, z; };
@@ -175,443 +123,60 @@ __device__ __forceinline__ void body_force(const float* Iw, V3 c, float m, V3 vw
     fv = add3(Iav, cf);
 }
 
-// Spatial inertia (-> ia_out[21]) and body force (-> f_out[6]) of body b from its frame and
-// its spatial velocity / acceleration (shared by the base and the hinge bodies).
-__device__ __noinline__ void body_inertia_force(const G1Tables& T, int b, Q4 quat, V3 pos, V3 p, V3 w, V3 v, V3 aw, V3 av,
-                                                float* ia_out, float* f_out) {
-    const V3 xip = add3(pos, qrot(quat, ld3(T.body_ipos + 3 * b)));
-    float Iw[9];
-    V3 c;
-    world_inertia(T, b, quat, xip, p, Iw, c);
-    const float m = T.body_mass[b];
-    spatial_inertia21(Iw, c, m, ia_out);
-    V3 fw, fv;
-    body_force(Iw, c, m, w, v, aw, av, fw, fv);
-    st3(f_out, fw);
-    st3(f_out + 3, fv);
-}
+// ------------------------------------------------------------------ frame layouts
+// A warp advances GW worlds together.  Each world has its own frame (WL) in shared memory;
+// the warp has one contact workspace (CL) that its worlds use one after another.
+constexpr int GW = 4;        // worlds per warp
+constexpr int CPW = 4;       // chain lanes per world in the tree sweeps (lane = 4 w + chain)
+static_assert(GW * CPW <= 32, "lanes");
 
-// The smooth part of the per-substep dynamics for the world in `fr` (qp, qv, tau filled):
-// forward kinematics, motion axes S, RNE bias, the articulated-inertia factor of M + dtB
-// and qacc_smooth = (M + dtB)^-1 (-bias + tau), written to MM row 0.
-//
-// Three sweeps over the chain decomposition of the tree, lane l walking chain l with the
-// running body state in registers (hand-offs through shared memory only at branch bodies):
-//   F1 (root->leaf): FK (dynamics.cuh:47-88), S (aba_bias.cuh:380-398), spatial inertias,
-//      RNE partial velocities / cdof_dot / accelerations (aba_bias.cuh:419-457) and body
-//      forces (aba_bias.cuh:458-466);
-//   B1 (leaf->root): subtree forces and bias (aba_bias.cuh:467-475), the articulated
-//      inertia factor (aba_factor.cuh:76-88) and, fused into the same pass, the bias-force
-//      sweep of the smooth solve (aba_factor.cuh:128-136); a body pulls its children's
-//      contributions in descending child index -- the order the reference pushes them;
-//   base: the floating base's 6x6 block and Cholesky solve (aba_factor.cuh:90-108,138-155);
-//   F2 (root->leaf): qdd per body (aba_factor.cuh:156-164).
-__device__ void warp_smooth(float* fr, const G1Tables& T, int lane, const float* bdt) {
-    using L = FrameLayout;
-    const float *qp = fr + L::QP, *qv = fr + L::QV, *tau = fr + L::TAU;
-    float *S = fr + L::S, *XPOS = fr + L::XPOS, *XQUAT = fr + L::XQUAT, *IAB = fr + L::IAB, *FOWN = fr + L::FOWN;
-    float *PAC = fr + L::PAC, *UB = fr + L::UB, *BST = fr + L::BST, *FU = fr + L::FU, *FINVD = fr + L::FINVD;
-    float* bias = fr + L::BIAS;
-    float* qacc_s = fr + L::MM;
-    const bool chain_lane = lane < T.nchain;
-
-    // ---- floating base (body 1): every chain lane computes it (identical values)
-    const V3 p = ld3(qp);
-    const Q4 q1 = qnormalize(ld4(qp + 3));
-    V3 bw = mk3(0, 0, 0), bv = mk3(0, 0, 0), baw = mk3(0, 0, 0), bav = mk3(-T.gravity[0], -T.gravity[1], -T.gravity[2]);
-    if (chain_lane) {
-        float R1[9];
-        qmat(q1, R1);
-        float Sb[6][6];
-#pragma unroll
-        for (int k = 0; k < 6; ++k)
-#pragma unroll
-            for (int i = 0; i < 6; ++i) Sb[k][i] = 0.f;
-        Sb[0][3] = 1.f; Sb[1][4] = 1.f; Sb[2][5] = 1.f;
-#pragma unroll
-        for (int k = 0; k < 3; ++k) { Sb[3 + k][0] = R1[k]; Sb[3 + k][1] = R1[3 + k]; Sb[3 + k][2] = R1[6 + k]; }
-        // RNE through the 6 base dofs (aba_bias.cuh:423-440)
-        V3 Sdw[6], Sdv[6];
-        V3 w = bw, v = bv;
-#pragma unroll
-        for (int a = 0; a < 3; ++a) {
-            const float qd = qv[a];
-            V3 sw = mk3(Sb[a][0], Sb[a][1], Sb[a][2]), sv = mk3(Sb[a][3], Sb[a][4], Sb[a][5]);
-            Sdw[a] = cross3(w, sw);
-            Sdv[a] = add3(cross3(w, sv), cross3(v, sw));
-            w = {w.x + sw.x * qd, w.y + sw.y * qd, w.z + sw.z * qd};
-            v = {v.x + sv.x * qd, v.y + sv.y * qd, v.z + sv.z * qd};
-        }
-        const V3 wr = w, vr = v;
-#pragma unroll
-        for (int a = 3; a < 6; ++a) {
-            V3 sw = mk3(Sb[a][0], Sb[a][1], Sb[a][2]), sv = mk3(Sb[a][3], Sb[a][4], Sb[a][5]);
-            Sdw[a] = cross3(wr, sw);
-            Sdv[a] = add3(cross3(wr, sv), cross3(vr, sw));
-        }
-#pragma unroll
-        for (int a = 3; a < 6; ++a) {
-            const float qd = qv[a];
-            w = {w.x + Sb[a][0] * qd, w.y + Sb[a][1] * qd, w.z + Sb[a][2] * qd};
-            v = {v.x + Sb[a][3] * qd, v.y + Sb[a][4] * qd, v.z + Sb[a][5] * qd};
-        }
-        V3 ea = baw, eb = bav;
-#pragma unroll
-        for (int a = 0; a < 6; ++a) {
-            const float qd = qv[a];
-            ea = {ea.x + Sdw[a].x * qd, ea.y + Sdw[a].y * qd, ea.z + Sdw[a].z * qd};
-            eb = {eb.x + Sdv[a].x * qd, eb.y + Sdv[a].y * qd, eb.z + Sdv[a].z * qd};
-        }
-        bw = w; bv = v; baw = ea; bav = eb;
-        if (lane == 0) {
-#pragma unroll
-            for (int k = 0; k < 6; ++k)
-#pragma unroll
-                for (int i = 0; i < 6; ++i) S[6 * k + i] = Sb[k][i];
-            st3(XPOS + 3, p);
-            st4(XQUAT + 4, q1);
-            body_inertia_force(T, 1, q1, p, p, bw, bv, baw, bav, IAB + 21, FOWN + 6);
-        }
-    }
-
-    // ---- F1: root -> leaf along the chains
-    {
-        V3 pos = p, w = bw, v = bv, aw = baw, av = bav;
-        Q4 quat = q1;
-        for (int s = 0; s < T.nsteps; ++s) {
-            const int k = chain_lane ? s - T.chain_start[lane] : -1;
-            if (k >= 0 && k < T.chain_len[lane]) {
-                const int b = T.chain_body[lane][k];
-                if (k == 0 && T.parent[b] != 1) {  // head below a branch body: its state from the slot
-                    const float* st = BST + 26 * T.branch_slot[T.parent[b]];
-                    pos = ld3(st); quat = ld4(st + 3); w = ld3(st + 7); v = ld3(st + 10); aw = ld3(st + 13); av = ld3(st + 16);
-                } else if (k == 0) {
-                    pos = p; quat = q1; w = bw; v = bv; aw = baw; av = bav;
-                }
-                const int j = T.body_jnt[b], d = T.dofadr[b];
-                // kinematics (hinge)
-                pos = add3(pos, qrot(quat, ld3(T.body_pos + 3 * b)));
-                quat = qmul(quat, ld4(T.body_quat + 4 * b));
-                const V3 an = ld3(T.jnt_pos + 3 * j), ax = ld3(T.jnt_axis + 3 * j);
-                const V3 anchor = add3(pos, qrot(quat, an));
-                float sn, cs;
-                sincosf(0.5f * qp[T.jnt_qposadr[j]], &sn, &cs);
-                quat = qmul(quat, Q4{cs, ax.x * sn, ax.y * sn, ax.z * sn});
-                pos = sub3(anchor, qrot(quat, an));
-                st3(XPOS + 3 * b, pos);
-                st4(XQUAT + 4 * b, quat);
-                // motion axis of the hinge dof
-                const V3 sw = qrot(quat, ax);
-                const V3 sv = cross3(sub3(add3(pos, qrot(quat, an)), p), sw);
-                st3(S + 6 * d, sw); st3(S + 6 * d + 3, sv);
-                // RNE forward (one dof)
-                const float qd = qv[d];
-                const V3 sdw = cross3(w, sw), sdv = add3(cross3(w, sv), cross3(v, sw));
-                w = {w.x + sw.x * qd, w.y + sw.y * qd, w.z + sw.z * qd};
-                v = {v.x + sv.x * qd, v.y + sv.y * qd, v.z + sv.z * qd};
-                aw = {aw.x + sdw.x * qd, aw.y + sdw.y * qd, aw.z + sdw.z * qd};
-                av = {av.x + sdv.x * qd, av.y + sdv.y * qd, av.z + sdv.z * qd};
-                body_inertia_force(T, b, quat, pos, p, w, v, aw, av, IAB + 21 * b, FOWN + 6 * b);
-                if (T.branch_slot[b] >= 0) {
-                    float* st = BST + 26 * T.branch_slot[b];
-                    st3(st, pos); st4(st + 3, quat); st3(st + 7, w); st3(st + 10, v); st3(st + 13, aw); st3(st + 16, av);
-                }
-            }
-            __syncwarp();
-        }
-    }
-
-    // ---- B1: leaf -> root along the chains (bias, factor, smooth-solve bias forces).  A body
-    // leaves its contributions (subtree force, IA - U U^T / D, pA + U ud) in its own slots,
-    // where its parent pulls them.
-    for (int s = 0; s < T.nsteps_back; ++s) {
-        const int k = chain_lane ? s - T.chain_bstart[lane] : -1;
-        const int len = chain_lane ? T.chain_len[lane] : 0;
-        if (k >= 0 && k < len) {
-            const int b = T.chain_body[lane][len - 1 - k], d = T.dofadr[b];
-            float f[6], ia[21], pa[6];
-#pragma unroll
-            for (int i = 0; i < 6; ++i) { f[i] = FOWN[6 * b + i]; pa[i] = 0.f; }
-#pragma unroll
-            for (int i = 0; i < 21; ++i) ia[i] = IAB[21 * b + i];
-            for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
-                const int c = T.child_list[q];
-#pragma unroll
-                for (int i = 0; i < 6; ++i) { f[i] += FOWN[6 * c + i]; pa[i] += PAC[6 * c + i]; }
-#pragma unroll
-                for (int i = 0; i < 21; ++i) ia[i] += IAB[21 * c + i];
-            }
-            float sd[6];
-#pragma unroll
-            for (int i = 0; i < 6; ++i) sd[i] = S[6 * d + i];
-            const float bd = sd[0] * f[0] + sd[1] * f[1] + sd[2] * f[2] + sd[3] * f[3] + sd[4] * f[4] + sd[5] * f[5];
-            bias[d] = bd;
-            const float rhs = -bd + tau[d];
-            float U[6];
-#pragma unroll
-            for (int r = 0; r < 6; ++r) {
-                float acc = 0.f;
-#pragma unroll
-                for (int c = 0; c < 6; ++c) acc += ia[sym6(r, c)] * sd[c];
-                U[r] = acc;
-            }
-            float D = 0.f;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) D += sd[i] * U[i];
-            D = D + T.armature[d];
-            if (bdt) D += bdt[d];
-            const float invD = 1.f / D;
-            float sp = 0.f;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) sp += sd[i] * pa[i];
-            const float u = rhs - sp;
-            const float ud = u * invD;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) FU[6 * b + i] = U[i];
-            FINVD[b] = invD;
-            UB[b] = u;
-#pragma unroll
-            for (int r = 0; r < 6; ++r)
-#pragma unroll
-                for (int c = r; c < 6; ++c) IAB[21 * b + sym6(r, c)] = ia[sym6(r, c)] - U[r] * U[c] * invD;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) { PAC[6 * b + i] = pa[i] + U[i] * ud; FOWN[6 * b + i] = f[i]; }
-        }
-        __syncwarp();
-    }
-
-    // ---- floating base: pull the pelvis children (descending), 6x6 block, Cholesky, qdd
-    const int b1 = 1;
-    if (lane < 21) {
-        float acc = IAB[21 * b1 + lane];
-        for (int q = T.child_start[b1]; q < T.child_start[b1 + 1]; ++q) acc += IAB[21 * T.child_list[q] + lane];
-        IAB[21 * b1 + lane] = acc;
-    } else if (lane < 27) {
-        const int i = lane - 21;
-        float acc = FOWN[6 * b1 + i];
-        for (int q = T.child_start[b1]; q < T.child_start[b1 + 1]; ++q) acc += FOWN[6 * T.child_list[q] + i];
-        FOWN[6 * b1 + i] = acc;
-    }
-    if (lane < 6) {
-        float acc = 0.f;
-        for (int q = T.child_start[b1]; q < T.child_start[b1 + 1]; ++q) acc += PAC[6 * T.child_list[q] + lane];
-        PAC[6 * b1 + lane] = acc;
-    }
-    __syncwarp();
-    float *U6 = fr + L::FU6, *L6 = fr + L::FL6;
-    for (int e = lane; e < 36; e += 32) {  // U6[i*6+l] = (IA S_l)[i]
-        const int i = e / 6, l = e % 6;
-        float acc = 0.f;
-#pragma unroll
-        for (int j = 0; j < 6; ++j) acc += IAB[21 * b1 + sym6(i, j)] * S[6 * l + j];
-        U6[e] = acc;
-    }
-    float ub = 0.f;
-    if (lane < 6) {  // base bias and u = (-bias + tau) - S^T pA
-        const float* f = FOWN + 6 * b1;
-        const float* sd = S + 6 * lane;
-        const float bd = sd[0] * f[0] + sd[1] * f[1] + sd[2] * f[2] + sd[3] * f[3] + sd[4] * f[4] + sd[5] * f[5];
-        bias[lane] = bd;
-        float sp = 0.f;
-#pragma unroll
-        for (int i = 0; i < 6; ++i) sp += sd[i] * PAC[6 * b1 + i];
-        ub = (-bd + tau[lane]) - sp;
-    }
-    __syncwarp();
-    for (int e = lane; e < 36; e += 32) {  // Dm[k*6+l] = S_k . U6_l (+ diag)
-        const int kk = e / 6, l = e % 6;
-        float acc = 0.f;
-#pragma unroll
-        for (int i = 0; i < 6; ++i) acc += S[6 * kk + i] * U6[i * 6 + l];
-        L6[e] = acc + (kk == l ? (T.armature[kk] + (bdt ? bdt[kk] : 0.f)) : 0.f);
-    }
-    __syncwarp();
-    float q[6];
-#pragma unroll
-    for (int k = 0; k < 6; ++k) q[k] = __shfl_sync(FULLMASK, ub, k);
-    if (lane == 0) {
-        float* Dm = L6;  // in place (aba_factor.cuh:103-107), rolled loops: one lane, once per substep
-#pragma unroll 1
-        for (int i = 0; i < 6; ++i)
-#pragma unroll 1
-            for (int j = 0; j <= i; ++j) {
-                float acc = Dm[i * 6 + j];
-                for (int k = 0; k < j; ++k) acc -= Dm[i * 6 + k] * Dm[j * 6 + k];
-                if (i == j) Dm[i * 6 + i] = sqrtf(acc); else Dm[i * 6 + j] = acc / Dm[j * 6 + j];
-            }
-#pragma unroll 1
-        for (int i = 0; i < 6; ++i) {
-            float acc = q[i];
-            for (int k = 0; k < i; ++k) acc -= Dm[i * 6 + k] * q[k];
-            q[i] = acc / Dm[i * 6 + i];
-        }
-#pragma unroll 1
-        for (int i = 5; i >= 0; --i) {
-            float acc = q[i];
-            for (int k = i + 1; k < 6; ++k) acc -= Dm[k * 6 + i] * q[k];
-            q[i] = acc / Dm[i * 6 + i];
-        }
-#pragma unroll
-        for (int k = 0; k < 6; ++k) qacc_s[k] = q[k];
-        float* A1 = fr + L::A1;
-#pragma unroll
-        for (int i = 0; i < 6; ++i) {
-            float acc = 0.f;
-#pragma unroll
-            for (int k = 0; k < 6; ++k) acc += S[6 * k + i] * q[k];
-            A1[i] = acc;
-        }
-    }
-    __syncwarp();
-
-    // ---- F2: root -> leaf, qdd per hinge body
-    {
-        float a[6];
-        for (int s = 0; s < T.nsteps; ++s) {
-            const int k = chain_lane ? s - T.chain_start[lane] : -1;
-            if (k >= 0 && k < T.chain_len[lane]) {
-                const int b = T.chain_body[lane][k], d = T.dofadr[b];
-                if (k == 0) {
-                    const int par = T.parent[b];
-                    const float* src = par == 1 ? fr + L::A1 : BST + 26 * T.branch_slot[par] + 19;
-#pragma unroll
-                    for (int i = 0; i < 6; ++i) a[i] = src[i];
-                }
-                float s2 = 0.f;
-#pragma unroll
-                for (int i = 0; i < 6; ++i) s2 += FU[6 * b + i] * a[i];
-                const float qdd = (UB[b] - s2) * FINVD[b];
-                qacc_s[d] = qdd;
-#pragma unroll
-                for (int i = 0; i < 6; ++i) a[i] = a[i] + S[6 * d + i] * qdd;
-                if (T.branch_slot[b] >= 0) {
-                    float* st = BST + 26 * T.branch_slot[b] + 19;
-#pragma unroll
-                    for (int i = 0; i < 6; ++i) st[i] = a[i];
-                }
-            }
-            __syncwarp();
-        }
-    }
-}
-
-// ------------------------------------------------------------------ M^-1 apply, one lane
-// y = (M + dtB)^-1 x in place on xy[0..NV), one lane per right-hand side, reading the factor
-// from the frame (every lane touches the same factor entry at the same time: a shared-memory
-// broadcast).  aba_factor.cuh:121-165.
-// The lane walks the chains with the articulated bias force of the current body in
-// registers.  Leaf->root, chains go last-to-first; a chain's head leaves its contribution in
-// hand[chain] and a body pulls its children's contributions in descending child index (the
-// order in which the reference's b-descending loop pushes them).  u_b = x_d - S_d.pA_b parks
-// in xy[d] between the sweeps.  Root->leaf, chains go first-to-last and a branch body leaves
-// its spatial acceleration in fwd[slot] for the chains below it.
-// `scratch`: this lane's 6*(MAXCHAIN + MAXBRANCH) floats.
-constexpr int SOLVE_SCRATCH = 6 * (G1_MAXCHAIN + G1_MAXBRANCH);
-static_assert(3 * MAXCON * SOLVE_SCRATCH <= FrameLayout::U1_END - FrameLayout::UNION,
-              "per-lane solve scratch must fit in the tree-sweep part of the frame union");
-__device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, float* xy, float* scratch) {
-    using L = FrameLayout;
-    const float *S = fr + L::S, *FU = fr + L::FU, *FINVD = fr + L::FINVD, *L6 = fr + L::FL6;
-    float* hand = scratch;
-    float* fwd = scratch + 6 * G1_MAXCHAIN;
-    // leaf -> root
-    for (int c = T.nchain - 1; c >= 0; --c) {
-        const int len = T.chain_len[c];
-        float pa[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        int carried = -1;
-        for (int k = len - 1; k >= 0; --k) {
-            const int b = T.chain_body[c][k], d = T.dofadr[b];
-            float acc[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
-                const int ch = T.child_list[q];
-                if (ch == carried) {
-#pragma unroll
-                    for (int i = 0; i < 6; ++i) acc[i] += pa[i];
-                } else {
-                    const float* src = hand + 6 * T.head_chain[ch];
-#pragma unroll
-                    for (int i = 0; i < 6; ++i) acc[i] += src[i];
-                }
-            }
-            const float* sd = S + 6 * d;
-            const float sp = ((((0.f + sd[0] * acc[0]) + sd[1] * acc[1]) + sd[2] * acc[2]) + sd[3] * acc[3]) + sd[4] * acc[4] + sd[5] * acc[5];
-            const float u = xy[d] - sp;
-            xy[d] = u;
-            const float ud = u * FINVD[b];
-            const float* U = FU + 6 * b;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) pa[i] = acc[i] + U[i] * ud;
-            carried = b;
-        }
-#pragma unroll
-        for (int i = 0; i < 6; ++i) hand[6 * c + i] = pa[i];
-    }
-    // floating base: pull the pelvis children, 6x6 Cholesky solve, base acceleration
-    const int d1 = T.dofadr[1];
-    float pa1[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int q = T.child_start[1]; q < T.child_start[2]; ++q) {
-        const float* src = hand + 6 * T.head_chain[T.child_list[q]];
-#pragma unroll
-        for (int i = 0; i < 6; ++i) pa1[i] += src[i];
-    }
-    float q6[6];
-#pragma unroll
-    for (int k = 0; k < 6; ++k) {
-        const float* sd = S + 6 * (d1 + k);
-        q6[k] = xy[d1 + k] - (((((0.f + sd[0] * pa1[0]) + sd[1] * pa1[1]) + sd[2] * pa1[2]) + sd[3] * pa1[3]) + sd[4] * pa1[4] + sd[5] * pa1[5]);
-    }
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        float acc = q6[i];
-#pragma unroll
-        for (int k = 0; k < i; ++k) acc -= L6[i * 6 + k] * q6[k];
-        q6[i] = acc / L6[i * 6 + i];
-    }
-#pragma unroll
-    for (int i = 5; i >= 0; --i) {
-        float acc = q6[i];
-#pragma unroll
-        for (int k = i + 1; k < 6; ++k) acc -= L6[k * 6 + i] * q6[k];
-        q6[i] = acc / L6[i * 6 + i];
-    }
-    float a1[6];
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        float acc = 0.f;
-#pragma unroll
-        for (int k = 0; k < 6; ++k) acc += S[6 * (d1 + k) + i] * q6[k];
-        a1[i] = acc;
-    }
-#pragma unroll
-    for (int k = 0; k < 6; ++k) xy[d1 + k] = q6[k];
-    // root -> leaf
-    for (int c = 0; c < T.nchain; ++c) {
-        const int par = T.parent[T.chain_body[c][0]];
-        float a[6];
-        if (par == 1) {
-#pragma unroll
-            for (int i = 0; i < 6; ++i) a[i] = a1[i];
-        } else {
-            const float* src = fwd + 6 * T.branch_slot[par];
-#pragma unroll
-            for (int i = 0; i < 6; ++i) a[i] = src[i];
-        }
-        for (int k = 0; k < T.chain_len[c]; ++k) {
-            const int b = T.chain_body[c][k], d = T.dofadr[b];
-            const float* U = FU + 6 * b;
-            const float s2 = ((((0.f + U[0] * a[0]) + U[1] * a[1]) + U[2] * a[2]) + U[3] * a[3]) + U[4] * a[4] + U[5] * a[5];
-            const float qdd = (xy[d] - s2) * FINVD[b];
-            xy[d] = qdd;
-            const float* sd = S + 6 * d;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) a[i] = a[i] + sd[i] * qdd;
-            if (T.branch_slot[b] >= 0) {
-                float* dst = fwd + 6 * T.branch_slot[b];
-#pragma unroll
-                for (int i = 0; i < 6; ++i) dst[i] = a[i];
-            }
-        }
-    }
+struct WL {  // per-world frame, offsets in floats
+    enum : int {
+        QP = 0,               // qpos [36]
+        QV = 36,              // qvel [35] (+1)
+        TGT = 72,             // PD targets [29] (+3)
+        TAU = 104,            // generalised force [35] (+1)
+        QACC = 140,           // qacc_smooth, then qacc [35] (+1)
+        S = 176,              // motion axes [35][6]
+        FU = 386,             // factor U [31][6]
+        FINVD = 572,          // factor 1/D [31] (+1)
+        FU6 = 604,            // base U6 [36]
+        FL6 = 640,            // base Dm -> Cholesky factor [36]
+        XS = 676,             // kept body frames (pelvis, feet): quat [4] + pos [3] (+1) per slot
+        BQ = 708,             // per body: quat [4] + (xipos - p) [3]  (F1 -> B1)
+        FOWN = 928,           // per body: own force, then subtree force [31][6]
+        UB = 1114,            // per body: u_b [31] (+1)
+        HF = 1146,            // F1 branch hand-off: pos, quat, w, v, aw, av [19] (+1) per branch slot
+        HA = HF + 20 * G1_MAXBRANCH,   // F2 branch hand-off: spatial acceleration [6] (+2)
+        HB = HA + 8 * G1_MAXBRANCH,    // B1 chain-head contributions: IA [21], f [6], pA [6] (+3)
+        A1 = HB + 36 * 4,     // base spatial acceleration [6] (+2)
+        CON = A1 + 8,         // contacts: sphere (int) [8], pt [8][3], pen [8]
+        MISC = CON + 40,      // [0] ncon (int)
+        SIZE = MISC + 4
+    };
+};
+struct CL {  // per-warp contact workspace, offsets in floats
+    enum : int {
+        MM = 0,                       // M^-1 of the 3 ncon basis rows [24][35]
+        EB = MM + 3 * G1_MAXCON * 35, // basis rows [8][3][12]
+        RR = EB + 288,                // R [32]
+        BV = RR + 32,                 // b [32]
+        FF = BV + 32,                 // f [32]
+        GRAM = FF + 32,               // 3x3 Gram blocks [36][9]
+        AP = GRAM + 324,              // Delassus matrix, packed upper triangle [528]
+        SCR_END = GRAM + 24 * 36,     // per-lane back-solve scratch aliases GRAM/AP (24 lanes x 36)
+        SIZE = (AP + 528 > SCR_END) ? AP + 528 : SCR_END
+    };
+};
+constexpr int WFLOATS = (WL::SIZE + 3) & ~3;
+constexpr int CFLOATS = (CL::SIZE + 3) & ~3;
+constexpr int GROUP_FLOATS = GW * WFLOATS + CFLOATS;
+constexpr int MSTR = 35;
+constexpr int SOLVE_SCRATCH = 6 * (4 + G1_MAXBRANCH);  // per solving lane, aliases GRAM/AP
+static_assert(3 * G1_MAXCON * SOLVE_SCRATCH <= CL::SIZE - CL::GRAM, "solve scratch must fit in GRAM/AP");
+__device__ __forceinline__ int apidx(int i, int j) {  // packed upper triangle of a 32x32 symmetric matrix
+    int a = min(i, j), b = max(i, j);
+    return a * 32 - (a * (a - 1)) / 2 + (b - a);
 }
 
 // ------------------------------------------------------------------ profiling (G1_PROF builds)
@@ -628,13 +193,492 @@ __device__ unsigned long long g_prof[16];
 #define PROF_BEGIN()
 #define PROF_MARK(i) do { } while (0)
 #endif
-enum ProfPhase { P_POLICY = 0, P_FK, P_AXES, P_BIAS, P_FACTOR, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_NPHASE };
+enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_NPHASE };
 
 // pyramid coefficients d_k = DC[k] of the 3-basis (env_qacc.cuh:98-100,154-155)
 __device__ __forceinline__ float dcoef(int k, int a) {
     if (a == 0) return 1.f;
     if (a == 1) return k == 0 ? 1.f : (k == 1 ? -1.f : 0.f);
     return k == 2 ? 1.f : (k == 3 ? -1.f : 0.f);
+}
+
+// ------------------------------------------------------------------ tree sweeps
+// body force of body b from its frame and spatial velocity / acceleration
+__device__ __forceinline__ void body_force_at(const G1Tables& T, int b, Q4 quat, V3 cpos, V3 w, V3 v, V3 aw, V3 av, float* f_out) {
+    float Iw[9];
+    V3 c;
+    world_inertia(T, b, quat, cpos, mk3(0, 0, 0), Iw, c);
+    V3 fw, fv;
+    body_force(Iw, c, T.body_mass[b], w, v, aw, av, fw, fv);
+    st3(f_out, fw);
+    st3(f_out + 3, fv);
+}
+// spatial inertia (packed 21) of body b from its orientation and com offset from the pelvis
+__device__ __forceinline__ void body_ia_at(const G1Tables& T, int b, Q4 quat, V3 cpos, float* ia) {
+    float Iw[9];
+    V3 c;
+    world_inertia(T, b, quat, cpos, mk3(0, 0, 0), Iw, c);
+    spatial_inertia21(Iw, c, T.body_mass[b], ia);
+}
+
+// The smooth part of the per-substep dynamics for the GW worlds of a warp (qp, qv, tau in each
+// world frame): forward kinematics, motion axes S, RNE bias, the articulated-inertia factor
+// of M + dtB and qacc_smooth = (M + dtB)^-1 (-bias + tau) into QACC.
+//
+// Lane 4w + l walks chain l of world w with the running body state in registers; hand-offs
+// through shared memory only at branch bodies.  Sweeps:
+//   F1 (root->leaf): FK (dynamics.cuh:47-88), S (aba_bias.cuh:380-398), RNE partial
+//      velocities / cdof_dot / accelerations (aba_bias.cuh:419-457), body forces (:458-466);
+//   B1 (leaf->root): subtree forces -> bias (aba_bias.cuh:467-475), the articulated-inertia
+//      factor (aba_factor.cuh:76-88) and, fused, the bias-force pass of the smooth solve
+//      (aba_factor.cuh:128-136).  A body adds its children's contributions in descending
+//      child index -- the order in which the reference's b-descending loops push them;
+//   base: the floating base's 6x6 block, its Cholesky solve (aba_factor.cuh:90-108,138-155);
+//   F2 (root->leaf): qdd per hinge body (aba_factor.cuh:156-164).
+// bias_out (optional, per world slot, global memory) receives qfrc_bias.
+__device__ void group_smooth(float* grp, const G1Tables& T, int lane, const float* const* bdt_w, float* const* bias_out) {
+    const int w = lane >> 2, cl = lane & 3;
+    const float* bdt = (bdt_w && w < GW) ? bdt_w[w] : nullptr;
+    const bool on = w < GW && cl < T.nchain;
+    float* fr = grp + (w < GW ? w : 0) * WFLOATS;
+    const float *qp = fr + WL::QP, *qv = fr + WL::QV, *tau = fr + WL::TAU;
+    float *S = fr + WL::S, *BQ = fr + WL::BQ, *FOWN = fr + WL::FOWN, *UB = fr + WL::UB;
+    float *FU = fr + WL::FU, *FINVD = fr + WL::FINVD, *qacc = fr + WL::QACC, *XS = fr + WL::XS;
+    float* bias = (bias_out && w < GW) ? bias_out[w] : nullptr;
+    PROF_BEGIN();
+
+    // ---- floating base (body 1): the chain lanes of a world compute it redundantly
+    const V3 p = ld3(qp);
+    const Q4 q1 = qnormalize(ld4(qp + 3));
+    V3 bw = mk3(0, 0, 0), bv = mk3(0, 0, 0), baw = mk3(0, 0, 0), bav = mk3(-T.gravity[0], -T.gravity[1], -T.gravity[2]);
+    if (on) {
+        float R1[9];
+        qmat(q1, R1);
+        // base motion axes: translation e_k, rotation = columns of R1
+        V3 Sw[6], Sv[6];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            Sw[k] = mk3(0, 0, 0);
+            Sv[k] = mk3(k == 0 ? 1.f : 0.f, k == 1 ? 1.f : 0.f, k == 2 ? 1.f : 0.f);
+            Sw[3 + k] = mk3(R1[k], R1[3 + k], R1[6 + k]);
+            Sv[3 + k] = mk3(0, 0, 0);
+        }
+        // RNE through the 6 base dofs (aba_bias.cuh:423-440)
+        V3 Sdw[6], Sdv[6];
+        V3 wv = bw, vv = bv;
+#pragma unroll
+        for (int a = 0; a < 3; ++a) {
+            const float qd = qv[a];
+            Sdw[a] = cross3(wv, Sw[a]);
+            Sdv[a] = add3(cross3(wv, Sv[a]), cross3(vv, Sw[a]));
+            wv = {wv.x + Sw[a].x * qd, wv.y + Sw[a].y * qd, wv.z + Sw[a].z * qd};
+            vv = {vv.x + Sv[a].x * qd, vv.y + Sv[a].y * qd, vv.z + Sv[a].z * qd};
+        }
+        const V3 wr = wv, vr = vv;
+#pragma unroll
+        for (int a = 3; a < 6; ++a) {
+            Sdw[a] = cross3(wr, Sw[a]);
+            Sdv[a] = add3(cross3(wr, Sv[a]), cross3(vr, Sw[a]));
+        }
+#pragma unroll
+        for (int a = 3; a < 6; ++a) {
+            const float qd = qv[a];
+            wv = {wv.x + Sw[a].x * qd, wv.y + Sw[a].y * qd, wv.z + Sw[a].z * qd};
+            vv = {vv.x + Sv[a].x * qd, vv.y + Sv[a].y * qd, vv.z + Sv[a].z * qd};
+        }
+        V3 ea = baw, eb = bav;
+#pragma unroll
+        for (int a = 0; a < 6; ++a) {
+            const float qd = qv[a];
+            ea = {ea.x + Sdw[a].x * qd, ea.y + Sdw[a].y * qd, ea.z + Sdw[a].z * qd};
+            eb = {eb.x + Sdv[a].x * qd, eb.y + Sdv[a].y * qd, eb.z + Sdv[a].z * qd};
+        }
+        bw = wv; bv = vv; baw = ea; bav = eb;
+        if (cl == 0) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) { st3(S + 6 * k, Sw[k]); st3(S + 6 * k + 3, Sv[k]); }
+            float* xs = XS + 8 * T.xslot[1];
+            st4(xs, q1); st3(xs + 4, p);
+            const V3 cpos = sub3(add3(p, qrot(q1, ld3(T.body_ipos + 3))), p);  // xipos - p, as the reference rounds it
+            st4(BQ + 7, q1); st3(BQ + 11, cpos);
+            body_force_at(T, 1, q1, cpos, bw, bv, baw, bav, FOWN + 6);
+        }
+    }
+
+    // ---- F1: root -> leaf along the chains
+    {
+        V3 pos = p, wv = bw, vv = bv, aw = baw, av = bav;
+        Q4 quat = q1;
+        for (int s = 0; s < T.nsteps; ++s) {
+            const int k = on ? s - T.chain_start[cl] : -1;
+            if (k >= 0 && k < T.chain_len[cl]) {
+                const int b = T.chain_body[cl][k];
+                if (k == 0) {
+                    const int par = T.parent[b];
+                    if (par == 1) {
+                        pos = p; quat = q1; wv = bw; vv = bv; aw = baw; av = bav;
+                    } else {
+                        const float* st = fr + WL::HF + 20 * T.branch_slot[par];
+                        pos = ld3(st); quat = ld4(st + 3); wv = ld3(st + 7); vv = ld3(st + 10); aw = ld3(st + 13); av = ld3(st + 16);
+                    }
+                }
+                const int j = T.body_jnt[b], d = T.dofadr[b];
+                pos = add3(pos, qrot(quat, ld3(T.body_pos + 3 * b)));
+                quat = qmul(quat, ld4(T.body_quat + 4 * b));
+                const V3 an = ld3(T.jnt_pos + 3 * j), ax = ld3(T.jnt_axis + 3 * j);
+                const V3 anchor = add3(pos, qrot(quat, an));
+                float sn, cs;
+                sincosf(0.5f * qp[T.jnt_qposadr[j]], &sn, &cs);
+                quat = qmul(quat, Q4{cs, ax.x * sn, ax.y * sn, ax.z * sn});
+                pos = sub3(anchor, qrot(quat, an));
+                if (T.xslot[b] >= 0) {
+                    float* xs = XS + 8 * T.xslot[b];
+                    st4(xs, quat); st3(xs + 4, pos);
+                }
+                const V3 cpos = sub3(add3(pos, qrot(quat, ld3(T.body_ipos + 3 * b))), p);
+                st4(BQ + 7 * b, quat); st3(BQ + 7 * b + 4, cpos);
+                const V3 sw = qrot(quat, ax);
+                const V3 sv = cross3(sub3(add3(pos, qrot(quat, an)), p), sw);
+                st3(S + 6 * d, sw); st3(S + 6 * d + 3, sv);
+                const float qd = qv[d];
+                const V3 sdw = cross3(wv, sw), sdv = add3(cross3(wv, sv), cross3(vv, sw));
+                wv = {wv.x + sw.x * qd, wv.y + sw.y * qd, wv.z + sw.z * qd};
+                vv = {vv.x + sv.x * qd, vv.y + sv.y * qd, vv.z + sv.z * qd};
+                aw = {aw.x + sdw.x * qd, aw.y + sdw.y * qd, aw.z + sdw.z * qd};
+                av = {av.x + sdv.x * qd, av.y + sdv.y * qd, av.z + sdv.z * qd};
+                body_force_at(T, b, quat, cpos, wv, vv, aw, av, FOWN + 6 * b);
+                if (T.branch_slot[b] >= 0) {
+                    float* st = fr + WL::HF + 20 * T.branch_slot[b];
+                    st3(st, pos); st4(st + 3, quat); st3(st + 7, wv); st3(st + 10, vv); st3(st + 13, aw); st3(st + 16, av);
+                }
+            }
+            __syncwarp();
+        }
+    }
+    PROF_MARK(P_F1);
+
+    // ---- B1: leaf -> root along the chains.  The contribution of the previous (child) body
+    // of the chain is carried in registers; other children (chain heads below a branch body)
+    // left theirs in HB.
+    {
+        float cia[21], cf[6], cpa[6];
+        int carried = -1;
+        for (int s = 0; s < T.nsteps_back; ++s) {
+            const int len = on ? T.chain_len[cl] : 0;
+            const int k = on ? s - T.chain_bstart[cl] : -1;
+            if (k >= 0 && k < len) {
+                const int b = T.chain_body[cl][len - 1 - k], d = T.dofadr[b];
+                float ia[21], f[6], pa[6];
+                body_ia_at(T, b, ld4(BQ + 7 * b), ld3(BQ + 7 * b + 4), ia);
+#pragma unroll
+                for (int i = 0; i < 6; ++i) { f[i] = FOWN[6 * b + i]; pa[i] = 0.f; }
+                for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
+                    const int c = T.child_list[q];
+                    if (c == carried) {
+#pragma unroll
+                        for (int i = 0; i < 21; ++i) ia[i] += cia[i];
+#pragma unroll
+                        for (int i = 0; i < 6; ++i) { f[i] += cf[i]; pa[i] += cpa[i]; }
+                    } else {
+                        const float* hb = fr + WL::HB + 36 * T.head_chain[c];
+#pragma unroll
+                        for (int i = 0; i < 21; ++i) ia[i] += hb[i];
+#pragma unroll
+                        for (int i = 0; i < 6; ++i) { f[i] += hb[21 + i]; pa[i] += hb[27 + i]; }
+                    }
+                }
+                float sd[6];
+#pragma unroll
+                for (int i = 0; i < 6; ++i) sd[i] = S[6 * d + i];
+                const float bd = sd[0] * f[0] + sd[1] * f[1] + sd[2] * f[2] + sd[3] * f[3] + sd[4] * f[4] + sd[5] * f[5];
+                if (bias) bias[d] = bd;
+                const float rhs = -bd + tau[d];
+                float U[6];
+#pragma unroll
+                for (int r = 0; r < 6; ++r) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int c = 0; c < 6; ++c) acc += ia[sym6(r, c)] * sd[c];
+                    U[r] = acc;
+                }
+                float D = 0.f;
+#pragma unroll
+                for (int i = 0; i < 6; ++i) D += sd[i] * U[i];
+                D = D + T.armature[d];
+                if (bdt) D += bdt[d];
+                const float invD = 1.f / D;
+                float sp = 0.f;
+#pragma unroll
+                for (int i = 0; i < 6; ++i) sp += sd[i] * pa[i];
+                const float u = rhs - sp;
+                const float ud = u * invD;
+#pragma unroll
+                for (int i = 0; i < 6; ++i) FU[6 * b + i] = U[i];
+                FINVD[b] = invD;
+                UB[b] = u;
+#pragma unroll
+                for (int r = 0; r < 6; ++r)
+#pragma unroll
+                    for (int c = r; c < 6; ++c) cia[sym6(r, c)] = ia[sym6(r, c)] - U[r] * U[c] * invD;
+#pragma unroll
+                for (int i = 0; i < 6; ++i) { cpa[i] = pa[i] + U[i] * ud; cf[i] = f[i]; }
+                carried = b;
+                if (k == len - 1) {  // chain head: leave the contribution for its parent
+                    float* hb = fr + WL::HB + 36 * cl;
+#pragma unroll
+                    for (int i = 0; i < 21; ++i) hb[i] = cia[i];
+#pragma unroll
+                    for (int i = 0; i < 6; ++i) { hb[21 + i] = cf[i]; hb[27 + i] = cpa[i]; }
+                }
+            }
+            __syncwarp();
+        }
+    }
+    PROF_MARK(P_B1);
+
+    // ---- floating base.  Lanes 4w..4w+3 of world w.
+    float* U6 = fr + WL::FU6;
+    float* L6 = fr + WL::FL6;
+    float base_ia[21], base_f[6], base_pa[6];
+    if (w < GW) {
+        // every lane of the world pulls the pelvis children (descending) into registers
+        body_ia_at(T, 1, ld4(BQ + 7), ld3(BQ + 11), base_ia);
+#pragma unroll
+        for (int i = 0; i < 6; ++i) { base_f[i] = FOWN[6 + i]; base_pa[i] = 0.f; }
+        for (int q = T.child_start[1]; q < T.child_start[2]; ++q) {
+            const float* hb = fr + WL::HB + 36 * T.head_chain[T.child_list[q]];
+#pragma unroll
+            for (int i = 0; i < 21; ++i) base_ia[i] += hb[i];
+#pragma unroll
+            for (int i = 0; i < 6; ++i) { base_f[i] += hb[21 + i]; base_pa[i] += hb[27 + i]; }
+        }
+        // U6[i*6+l] = (IA S_l)[i]: lane cl computes columns l = cl, cl+4 (< 6)
+        for (int l = cl; l < 6; l += 4)
+#pragma unroll
+            for (int i = 0; i < 6; ++i) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < 6; ++j) acc += base_ia[sym6(i, j)] * S[6 * l + j];
+                U6[i * 6 + l] = acc;
+            }
+    }
+    __syncwarp();
+    float q6[6];
+    if (w < GW) {
+        // Dm[k*6+l] = S_k . U6_l (+ diag); lane cl: rows k = cl, cl+4
+        for (int kk = cl; kk < 6; kk += 4)
+#pragma unroll
+            for (int l = 0; l < 6; ++l) {
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < 6; ++i) acc += S[6 * kk + i] * U6[i * 6 + l];
+                L6[kk * 6 + l] = acc + (kk == l ? (T.armature[kk] + (bdt ? bdt[kk] : 0.f)) : 0.f);
+            }
+        // base bias and u = (-bias + tau) - S^T pA (all 6, every lane of the world)
+#pragma unroll
+        for (int kk = 0; kk < 6; ++kk) {
+            const float* sd = S + 6 * kk;
+            const float bd = sd[0] * base_f[0] + sd[1] * base_f[1] + sd[2] * base_f[2] + sd[3] * base_f[3] +
+                             sd[4] * base_f[4] + sd[5] * base_f[5];
+            if (bias && cl == 0) bias[kk] = bd;
+            float sp = 0.f;
+#pragma unroll
+            for (int i = 0; i < 6; ++i) sp += sd[i] * base_pa[i];
+            q6[kk] = (-bd + tau[kk]) - sp;
+        }
+    }
+    __syncwarp();
+    if (w < GW && cl == 0) {
+        float* Dm = L6;  // in-place Cholesky (aba_factor.cuh:103-107); one lane per world
+#pragma unroll 1
+        for (int i = 0; i < 6; ++i)
+#pragma unroll 1
+            for (int j = 0; j <= i; ++j) {
+                float acc = Dm[i * 6 + j];
+                for (int k = 0; k < j; ++k) acc -= Dm[i * 6 + k] * Dm[j * 6 + k];
+                if (i == j) Dm[i * 6 + i] = sqrtf(acc); else Dm[i * 6 + j] = acc / Dm[j * 6 + j];
+            }
+#pragma unroll 1
+        for (int i = 0; i < 6; ++i) {
+            float acc = q6[i];
+            for (int k = 0; k < i; ++k) acc -= Dm[i * 6 + k] * q6[k];
+            q6[i] = acc / Dm[i * 6 + i];
+        }
+#pragma unroll 1
+        for (int i = 5; i >= 0; --i) {
+            float acc = q6[i];
+            for (int k = i + 1; k < 6; ++k) acc -= Dm[k * 6 + i] * q6[k];
+            q6[i] = acc / Dm[i * 6 + i];
+        }
+#pragma unroll
+        for (int k = 0; k < 6; ++k) qacc[k] = q6[k];
+        float* A1 = fr + WL::A1;
+#pragma unroll
+        for (int i = 0; i < 6; ++i) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 6; ++k) acc += S[6 * k + i] * q6[k];
+            A1[i] = acc;
+        }
+    }
+    __syncwarp();
+    PROF_MARK(P_BASE);
+
+    // ---- F2: root -> leaf, qdd per hinge body
+    {
+        float a[6];
+        for (int s = 0; s < T.nsteps; ++s) {
+            const int k = on ? s - T.chain_start[cl] : -1;
+            if (k >= 0 && k < T.chain_len[cl]) {
+                const int b = T.chain_body[cl][k], d = T.dofadr[b];
+                if (k == 0) {
+                    const int par = T.parent[b];
+                    const float* src = par == 1 ? fr + WL::A1 : fr + WL::HA + 8 * T.branch_slot[par];
+#pragma unroll
+                    for (int i = 0; i < 6; ++i) a[i] = src[i];
+                }
+                float s2 = 0.f;
+#pragma unroll
+                for (int i = 0; i < 6; ++i) s2 += FU[6 * b + i] * a[i];
+                const float qdd = (UB[b] - s2) * FINVD[b];
+                qacc[d] = qdd;
+#pragma unroll
+                for (int i = 0; i < 6; ++i) a[i] = a[i] + S[6 * d + i] * qdd;
+                if (T.branch_slot[b] >= 0) {
+                    float* st = fr + WL::HA + 8 * T.branch_slot[b];
+#pragma unroll
+                    for (int i = 0; i < 6; ++i) st[i] = a[i];
+                }
+            }
+            __syncwarp();
+        }
+    }
+    PROF_MARK(P_F2);
+}
+
+// ------------------------------------------------------------------ M^-1 apply, one lane
+// y = (M + dtB)^-1 x in place on xy[0..NV), one lane per right-hand side, reading the factor
+// of world frame `fr` (a shared-memory broadcast: every lane reads the same entry).
+// aba_factor.cuh:121-165.  The lane walks the chains with the articulated bias force of the
+// current body in registers; leaf->root the chains go last-to-first and a chain head leaves
+// its contribution in hand[chain]; a body adds its children in descending child index.
+// u_b = x_d - S_d.pA_b parks in xy[d] between the sweeps; root->leaf a branch body leaves
+// its acceleration in fwd[slot].  `scratch`: SOLVE_SCRATCH floats of this lane.
+constexpr int MAXCL = 12;  // longest chain the unrolled solve handles
+__device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, float* xy, float* scratch) {
+    const float *S = fr + WL::S, *FU = fr + WL::FU, *FINVD = fr + WL::FINVD, *L6 = fr + WL::FL6;
+    float* hand = scratch;
+    float* fwd = scratch + 6 * 4;
+    // leaf -> root, chains last-to-first
+    for (int c = T.nchain - 1; c >= 0; --c) {
+        const int len = T.chain_len[c];
+        int bl[MAXCL];
+#pragma unroll
+        for (int k = 0; k < MAXCL; ++k) bl[k] = k < len ? T.chain_body[c][k] : 0;
+        float pa[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = MAXCL - 1; k >= 0; --k) {
+            if (k >= len) continue;
+            const int b = bl[k], d = T.dofadr[b];
+            float acc[6];
+            if (T.branch_slot[b] >= 0) {  // branch body: children in descending index
+#pragma unroll
+                for (int i = 0; i < 6; ++i) acc[i] = 0.f;
+                for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
+                    const int ch = T.child_list[q];
+                    if (k + 1 < len && ch == bl[(k + 1 < MAXCL) ? k + 1 : k]) {
+#pragma unroll
+                        for (int i = 0; i < 6; ++i) acc[i] += pa[i];
+                    } else {
+                        const float* src = hand + 6 * T.head_chain[ch];
+#pragma unroll
+                        for (int i = 0; i < 6; ++i) acc[i] += src[i];
+                    }
+                }
+            } else {  // one child (the next body of the chain) or a leaf
+#pragma unroll
+                for (int i = 0; i < 6; ++i) acc[i] = pa[i];
+            }
+            const float* sd = S + 6 * d;
+            const float sp = ((((0.f + sd[0] * acc[0]) + sd[1] * acc[1]) + sd[2] * acc[2]) + sd[3] * acc[3]) + sd[4] * acc[4] + sd[5] * acc[5];
+            const float u = xy[d] - sp;
+            xy[d] = u;
+            const float ud = u * FINVD[b];
+            const float* U = FU + 6 * b;
+#pragma unroll
+            for (int i = 0; i < 6; ++i) pa[i] = acc[i] + U[i] * ud;
+        }
+#pragma unroll
+        for (int i = 0; i < 6; ++i) hand[6 * c + i] = pa[i];
+    }
+    float pa1[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int q = T.child_start[1]; q < T.child_start[2]; ++q) {
+        const float* src = hand + 6 * T.head_chain[T.child_list[q]];
+#pragma unroll
+        for (int i = 0; i < 6; ++i) pa1[i] += src[i];
+    }
+    float q6[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+        const float* sd = S + 6 * k;
+        q6[k] = xy[k] - (((((0.f + sd[0] * pa1[0]) + sd[1] * pa1[1]) + sd[2] * pa1[2]) + sd[3] * pa1[3]) + sd[4] * pa1[4] + sd[5] * pa1[5]);
+    }
+#pragma unroll 1
+    for (int i = 0; i < 6; ++i) {
+        float acc = q6[i];
+        for (int k = 0; k < i; ++k) acc -= L6[i * 6 + k] * q6[k];
+        q6[i] = acc / L6[i * 6 + i];
+    }
+#pragma unroll 1
+    for (int i = 5; i >= 0; --i) {
+        float acc = q6[i];
+        for (int k = i + 1; k < 6; ++k) acc -= L6[k * 6 + i] * q6[k];
+        q6[i] = acc / L6[i * 6 + i];
+    }
+    float a1[6];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 6; ++k) acc += S[6 * k + i] * q6[k];
+        a1[i] = acc;
+    }
+#pragma unroll
+    for (int k = 0; k < 6; ++k) xy[k] = q6[k];
+    // root -> leaf, chains first-to-last
+    for (int c = 0; c < T.nchain; ++c) {
+        const int len = T.chain_len[c];
+        int bl[MAXCL];
+#pragma unroll
+        for (int k = 0; k < MAXCL; ++k) bl[k] = k < len ? T.chain_body[c][k] : 0;
+        const int par = T.parent[bl[0]];
+        float a[6];
+        if (par == 1) {
+#pragma unroll
+            for (int i = 0; i < 6; ++i) a[i] = a1[i];
+        } else {
+            const float* src = fwd + 6 * T.branch_slot[par];
+#pragma unroll
+            for (int i = 0; i < 6; ++i) a[i] = src[i];
+        }
+#pragma unroll
+        for (int k = 0; k < MAXCL; ++k) {
+            if (k >= len) continue;
+            const int b = bl[k], d = T.dofadr[b];
+            const float* U = FU + 6 * b;
+            const float s2 = ((((0.f + U[0] * a[0]) + U[1] * a[1]) + U[2] * a[2]) + U[3] * a[3]) + U[4] * a[4] + U[5] * a[5];
+            const float qdd = (xy[d] - s2) * FINVD[b];
+            xy[d] = qdd;
+            const float* sd = S + 6 * d;
+#pragma unroll
+            for (int i = 0; i < 6; ++i) a[i] = a[i] + sd[i] * qdd;
+            if (T.branch_slot[b] >= 0) {
+                float* dst = fwd + 6 * T.branch_slot[b];
+#pragma unroll
+                for (int i = 0; i < 6; ++i) dst[i] = a[i];
+            }
+        }
+    }
 }
 
 // ------------------------------------------------------------------ contact
@@ -653,221 +697,305 @@ __device__ __forceinline__ float foot_impedance(const G1Tables& T, float pos) {
 struct QaccOpts {
     int pgs_iters;
     float mu;
-    const float* bdt;  // shared-memory dt*B diagonal (may be null)
+    const float* const* bdt;  // per world slot: shared-memory dt*B diagonal (entries may be null)
 };
 
-// Full per-substep generalized acceleration for the world in `fr` (qp, qv, tau filled);
-// FK must have run.  env_qacc.cuh:27-212.  Writes qacc to fr[QACC]; f / ncon stay in the
-// frame.  Returns ncon.
-__device__ int warp_qacc(float* fr, const G1Tables& T, int lane, const QaccOpts& opt) {
-    using L = FrameLayout;
-    PROF_BEGIN();
-    warp_smooth(fr, T, lane, opt.bdt);
-    PROF_MARK(P_FACTOR);
-    const float* S = fr + L::S;
-    float* MM = fr + L::MM;
-    int* con_s = reinterpret_cast<int*>(fr + L::CON);
-    float *con_pt = fr + L::CON + 8, *con_pen = fr + L::CON + 32;
-    // foot spheres vs z=0, compacted in sphere order (contact.cuh:31-46)
+// Foot-sphere contacts of the GW worlds (contact.cuh:31-46), lane = 8 w + sphere, compacted
+// in sphere order into each world's CON; returns nothing, ncon in MISC[0].
+__device__ void group_detect(float* grp, const G1Tables& T, int lane) {
+    static_assert(GW * G1_NFOOT_ <= 32, "one lane per (world, sphere)");
+    const int w = lane / NFOOT, s = lane % NFOOT;
+    float* fr = grp + (w < GW ? w : 0) * WFLOATS;
     bool hit = false;
-    float cx = 0, cy = 0, pen = 0;
-    if (lane < NFOOT) {
-        int b = T.foot_body[lane];
-        const float* xp = fr + L::XPOS + 3 * b;
-        V3 c = add3(ld3(xp), qrot(ld4(fr + L::XQUAT + 4 * b), ld3(T.foot_lpos + 3 * lane)));
+    float cx = 0.f, cy = 0.f, pen = 0.f;
+    if (w < GW) {
+        const float* xs = fr + WL::XS + 8 * T.xslot[T.foot_body[s]];
+        const V3 c = add3(ld3(xs + 4), qrot(ld4(xs), ld3(T.foot_lpos + 3 * s)));
         pen = c.z - G1M_FOOT_RADIUS;
         hit = pen < 0.f;
         cx = c.x; cy = c.y;
     }
-    unsigned m = __ballot_sync(FULLMASK, hit);
-    int ncon = __popc(m);
+    const unsigned m = __ballot_sync(FULLMASK, hit);
+    const unsigned wm = (m >> (NFOOT * (w < GW ? w : 0))) & ((1u << NFOOT) - 1u);
     if (hit) {
-        int k = __popc(m & ((1u << lane) - 1u));
-        con_s[k] = lane;
-        con_pt[3 * k] = cx; con_pt[3 * k + 1] = cy; con_pt[3 * k + 2] = pen * 0.5f;
-        con_pen[k] = pen;
+        const int k = __popc(wm & ((1u << s) - 1u));
+        int* con_s = reinterpret_cast<int*>(fr + WL::CON);
+        con_s[k] = s;
+        fr[WL::CON + 8 + 3 * k] = cx; fr[WL::CON + 9 + 3 * k] = cy; fr[WL::CON + 10 + 3 * k] = pen * 0.5f;
+        fr[WL::CON + 32 + k] = pen;
     }
-    V3 p = ld3(fr + L::XPOS + 3);
-    // contact basis right-hand sides: rows 1..3ncon (zero-filled; row 0 holds qacc_smooth)
-    const int nrhs = 1 + 3 * ncon;
-    for (int e = MSTR + lane; e < nrhs * MSTR; e += 32) MM[e] = 0.f;
+    if (w < GW && s == 0) reinterpret_cast<int*>(fr + WL::MISC)[0] = __popc(wm);
     __syncwarp();
-    // contact basis rows e0 = n, e1 = mu t1, e2 = mu t2 over the ancestor dofs
-    // (env_qacc.cuh:113-126), one lane per (contact, dof)
-    float* EB = fr + L::EB;
-    for (int it = lane; it < ncon * CDS; it += 32) {
-        int c = it / CDS, k = it % CDS, s = con_s[c];
+}
+
+// A contact batch: worlds of the group (slot ids) whose contacts are solved together,
+// at most MAXCON contacts in total; contact gc of the batch belongs to world slot
+// wid[x] with coff[x] <= gc < coff[x+1].
+struct Batch {
+    int nw, wid[GW], coff[GW + 1];
+    __device__ __forceinline__ int world_of(int gc) const {
+        int x = 0;
+        while (x + 1 < nw && gc >= coff[x + 1]) ++x;
+        return x;
+    }
+};
+
+// Contact correction for the worlds of a batch by the whole warp, using the workspace cw:
+// qacc += M^-1 J' f per world  (env_qacc.cuh:53-211).  The worlds' constraint rows sit side
+// by side; the Delassus matrix is block diagonal over worlds and each world's PGS sweeps
+// its own rows in order, all worlds in the same pass.  f -> cw[FF] (world x's rows start at
+// 4*coff[x]).
+__device__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, const Batch& B) {
+    float* MM = cw + CL::MM;
+    float* EB = cw + CL::EB;
+    const int nc = B.coff[B.nw], nb = 3 * nc, nefc_all = 4 * nc;
+    PROF_BEGIN();
+    for (int e = lane; e < nb * MSTR; e += 32) MM[e] = 0.f;
+    __syncwarp();
+    // basis rows e0 = n, e1 = mu t1, e2 = mu t2 over the ancestor dofs (env_qacc.cuh:113-126)
+    for (int it = lane; it < nc * CDS; it += 32) {
+        const int gc = it / CDS, k = it % CDS, x = B.world_of(gc), c = gc - B.coff[x];
+        const float* fr = grp + B.wid[x] * WFLOATS;
+        const int s = reinterpret_cast<const int*>(fr + WL::CON)[c];
         if (k < T.foot_ndof[s]) {
-            int a = T.foot_dofs[s][k];
-            V3 r = sub3(ld3(con_pt + 3 * c), p);
-            V3 t = add3(cross3(ld3(S + 6 * a), r), ld3(S + 6 * a + 3));
-            float e0 = t.z, e1 = opt.mu * t.y, e2 = -opt.mu * t.x;
-            EB[c * 36 + k] = e0; EB[c * 36 + 12 + k] = e1; EB[c * 36 + 24 + k] = e2;
-            MM[(1 + 3 * c) * MSTR + a] = e0; MM[(2 + 3 * c) * MSTR + a] = e1; MM[(3 + 3 * c) * MSTR + a] = e2;
+            const int a = T.foot_dofs[s][k];
+            const float* S = fr + WL::S;
+            const V3 p = ld3(fr + WL::XS + 8 * T.xslot[1] + 4);
+            const V3 r = sub3(ld3(fr + WL::CON + 8 + 3 * c), p);
+            const V3 t = add3(cross3(ld3(S + 6 * a), r), ld3(S + 6 * a + 3));
+            const float e0 = t.z, e1 = opt.mu * t.y, e2 = -opt.mu * t.x;
+            EB[gc * 36 + k] = e0; EB[gc * 36 + 12 + k] = e1; EB[gc * 36 + 24 + k] = e2;
+            MM[(3 * gc) * MSTR + a] = e0; MM[(3 * gc + 1) * MSTR + a] = e1; MM[(3 * gc + 2) * MSTR + a] = e2;
         }
     }
     __syncwarp();
     PROF_MARK(P_CSETUP);
-    // all basis back-solves at once: lane r solves basis column r
-    if (lane < nrhs - 1) lane_solve(fr, T, MM + (lane + 1) * MSTR, fr + L::UNION + lane * SOLVE_SCRATCH);
+    if (lane < nb)
+        lane_solve(grp + B.wid[B.world_of(lane / 3)] * WFLOATS, T, MM + lane * MSTR, cw + CL::GRAM + lane * SOLVE_SCRATCH);
     __syncwarp();
     PROF_MARK(P_SOLVE);
-    float* qacc = fr + L::QACC;
-    if (ncon == 0) {
-        for (int d = lane; d < NV; d += 32) qacc[d] = MM[d];
-        __syncwarp();
-        return 0;
-    }
     // per contact: bb = e.qacc_smooth, e.qvel -> R, aref, b  (env_qacc.cuh:113-136, 188-191)
-    float *RR = fr + L::RR, *BV = fr + L::BV;
-    if (lane < ncon) {
-        int c = lane, s = con_s[c], nd = T.foot_ndof[s];
-        const float* qv = fr + L::QV;
+    float *RR = cw + CL::RR, *BV = cw + CL::BV;
+    if (lane < nc) {
+        const int gc = lane, x = B.world_of(gc), c = gc - B.coff[x];
+        const float* fr = grp + B.wid[x] * WFLOATS;
+        const int s = reinterpret_cast<const int*>(fr + WL::CON)[c], nd = T.foot_ndof[s];
+        const float *qs = fr + WL::QACC, *qv = fr + WL::QV;
         float b0 = 0, b1 = 0, b2 = 0, v0 = 0, v1 = 0, v2 = 0;
         for (int k = 0; k < nd; ++k) {
-            int a = T.foot_dofs[s][k];
-            float e0 = EB[c * 36 + k], e1 = EB[c * 36 + 12 + k], e2 = EB[c * 36 + 24 + k];
-            float qa = MM[a], qd = qv[a];
+            const int a = T.foot_dofs[s][k];
+            const float e0 = EB[gc * 36 + k], e1 = EB[gc * 36 + 12 + k], e2 = EB[gc * 36 + 24 + k];
+            const float qa = qs[a], qd = qv[a];
             b0 += e0 * qa; b1 += e1 * qa; b2 += e2 * qa;
             v0 += e0 * qd; v1 += e1 * qd; v2 += e2 * qd;
         }
-        float dmax = T.solimp[1], tc = T.solref[0], dr = T.solref[1];
-        float bcoef = 2.f / (dmax * tc);
-        float kcoef = 1.f / (dmax * dmax * tc * tc * dr * dr);
-        float pyr = (1.f + opt.mu * opt.mu) * (2.f * opt.mu * opt.mu / G1M_FOOT_IMPRATIO);
-        float pn = con_pen[c], imp = foot_impedance(T, pn);
-        float Rc = T.foot_invw0[s] * pyr * (1.f - imp) / imp;
-        float kip = kcoef * imp * pn;
-        float dv[4] = {v0 + v1, v0 - v1, v0 + v2, v0 - v2};
-        float db[4] = {b0 + b1, b0 - b1, b0 + b2, b0 - b2};
+        const float dmax = T.solimp[1], tc = T.solref[0], dr = T.solref[1];
+        const float bcoef = 2.f / (dmax * tc);
+        const float kcoef = 1.f / (dmax * dmax * tc * tc * dr * dr);
+        const float pyr = (1.f + opt.mu * opt.mu) * (2.f * opt.mu * opt.mu / G1M_FOOT_IMPRATIO);
+        const float pn = fr[WL::CON + 32 + c], imp = foot_impedance(T, pn);
+        const float Rc = T.foot_invw0[s] * pyr * (1.f - imp) / imp;
+        const float kip = kcoef * imp * pn;
+        const float dv[4] = {v0 + v1, v0 - v1, v0 + v2, v0 - v2};
+        const float db[4] = {b0 + b1, b0 - b1, b0 + b2, b0 - b2};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            float aref = -bcoef * dv[k] - kip;
-            RR[4 * c + k] = Rc;
-            BV[4 * c + k] = db[k] - aref;
+            const float aref = -bcoef * dv[k] - kip;
+            RR[4 * gc + k] = Rc;
+            BV[4 * gc + k] = db[k] - aref;
         }
     }
-    // 3x3 Gram blocks G[a][b] = e_{c,a} . m_{c',b} over c's dofs, c <= c'
-    // (env_qacc.cuh:161-171), one lane per (pair, a, b)
-    float* G = fr + L::GRAM;
-    const int npair = ncon * (ncon + 1) / 2;
+    // pairs (c <= c') inside each world of the batch
+    int poff[GW + 1];
+    poff[0] = 0;
+#pragma unroll
+    for (int x = 0; x < GW; ++x) {
+        const int n = x < B.nw ? B.coff[x + 1] - B.coff[x] : 0;
+        poff[x + 1] = poff[x] + n * (n + 1) / 2;
+    }
+    const int npair = poff[B.nw];
+    // 3x3 Gram blocks G[a][b] = e_{c,a} . m_{c',b} over c's dofs (env_qacc.cuh:161-171)
+    float* G = cw + CL::GRAM;
     for (int it = lane; it < npair * 9; it += 32) {
-        int pr = it / 9, ab = it % 9, a = ab / 3, bb = ab % 3;
-        int c = 0, rem = pr;
-        while (rem >= ncon - c) { rem -= ncon - c; ++c; }
-        int cp = c + rem, s = con_s[c], nd = T.foot_ndof[s];
-        const float* ea = EB + c * 36 + 12 * a;
-        const float* mcp = MM + (1 + 3 * cp + bb) * MSTR;
+        const int pr = it / 9, ab = it % 9, a = ab / 3, bb = ab % 3;
+        int x = 0;
+        while (x + 1 < B.nw && pr >= poff[x + 1]) ++x;
+        const int n = B.coff[x + 1] - B.coff[x];
+        int c = 0, rem = pr - poff[x];
+        while (rem >= n - c) { rem -= n - c; ++c; }
+        const int gc = B.coff[x] + c, gcp = B.coff[x] + c + rem;
+        const float* fr = grp + B.wid[x] * WFLOATS;
+        const int s = reinterpret_cast<const int*>(fr + WL::CON)[c], nd = T.foot_ndof[s];
+        const float* ea = EB + gc * 36 + 12 * a;
+        const float* mcp = MM + (3 * gcp + bb) * MSTR;
         float g = 0.f;
         for (int k = 0; k < nd; ++k) g += ea[k] * mcp[T.foot_dofs[s][k]];
         G[pr * 9 + ab] = g;
     }
     __syncwarp();
-    // Delassus A = J M^-1 J' + diag R: expand each Gram block to the 4x4 pyramid block
-    // (env_qacc.cuh:172-187), one lane per (pair, k)
-    float* A = fr + L::AMAT;
-    const int nefc = 4 * ncon;
+    // A = J M^-1 J' + diag R: each Gram block expanded to its 4x4 pyramid block
+    // (env_qacc.cuh:172-187), packed upper triangle
+    float* AP = cw + CL::AP;
     for (int it = lane; it < npair * 4; it += 32) {
-        int pr = it >> 2, k = it & 3;
-        int c = 0, rem = pr;
-        while (rem >= ncon - c) { rem -= ncon - c; ++c; }
-        int cp = c + rem;
+        const int pr = it >> 2, k = it & 3;
+        int x = 0;
+        while (x + 1 < B.nw && pr >= poff[x + 1]) ++x;
+        const int n = B.coff[x + 1] - B.coff[x];
+        int c = 0, rem = pr - poff[x];
+        while (rem >= n - c) { rem -= n - c; ++c; }
+        const int cp = c + rem;
         const float* g = G + 9 * pr;
         const float c0 = dcoef(k, 0), c1 = dcoef(k, 1), c2 = dcoef(k, 2);
-        float t0 = c0 * g[0] + c1 * g[3] + c2 * g[6];
-        float t1 = c0 * g[1] + c1 * g[4] + c2 * g[7];
-        float t2 = c0 * g[2] + c1 * g[5] + c2 * g[8];
-        int i = 4 * c + k;
-        // inside a diagonal block (c == cp) the reference writes (k,kp) and (kp,k) from both
-        // iterations and the later one (larger k) wins; this lane owns kp <= k only
+        const float t0 = c0 * g[0] + c1 * g[3] + c2 * g[6];
+        const float t1 = c0 * g[1] + c1 * g[4] + c2 * g[7];
+        const float t2 = c0 * g[2] + c1 * g[5] + c2 * g[8];
+        const int i = 4 * (B.coff[x] + c) + k;
+        // inside a diagonal block the reference's later (larger k) write of (k,kp)/(kp,k) wins
         const int kpmax = (c == cp) ? k : 3;
 #pragma unroll
         for (int kp = 0; kp < 4; ++kp) {
             if (kp > kpmax) break;
             float aij = t0 * dcoef(kp, 0) + t1 * dcoef(kp, 1) + t2 * dcoef(kp, 2);
-            int j = 4 * cp + kp;
+            const int j = 4 * (B.coff[x] + cp) + kp;
             if (i == j) aij += RR[i];
-            A[i * ASTR + j] = aij;
-            A[j * ASTR + i] = aij;
+            AP[apidx(i, j)] = aij;
         }
     }
     __syncwarp();
     PROF_MARK(P_GRAM);
-    // projected Gauss-Seidel, rows in order (contact.cuh:159-171).  Lane j keeps the
-    // residual r_j = b_j + sum_k A_jk f_k; after row i moves by delta, every lane updates
-    // its residual with column i of A.
-    float fj = 0.f, rj = lane < nefc ? BV[lane] : 0.f, ajj = lane < nefc ? A[lane * ASTR + lane] : 1.f;
-    float inv = 1.f / ajj;
+    // projected Gauss-Seidel, each world's rows in order (contact.cuh:159-171), the worlds side
+    // by side.  Lane j keeps the residual r_j = b_j + sum_k A_jk f_k of its row; after row i of
+    // its world moves by delta, it adds A_ji delta.
+    const int xj = lane < nefc_all ? B.world_of(lane / 4) : 0;
+    const int r0 = 4 * B.coff[xj], nrow = lane < nefc_all ? 4 * (B.coff[xj + 1] - B.coff[xj]) : 0;
+    int maxrow = 0;
+#pragma unroll
+    for (int x = 0; x < GW; ++x)
+        if (x < B.nw) maxrow = max(maxrow, 4 * (B.coff[x + 1] - B.coff[x]));
+    float fj = 0.f, rj = lane < nefc_all ? BV[lane] : 0.f;
+    const float ajj = lane < nefc_all ? AP[apidx(lane, lane)] : 1.f;
+    const float inv = 1.f / ajj;
+    const int lj = lane - r0;
     for (int itr = 0; itr < opt.pgs_iters; ++itr) {
-        for (int i = 0; i < nefc; ++i) {
-            float aji = lane < nefc ? A[i * ASTR + lane] : 0.f;
+        for (int i = 0; i < maxrow; ++i) {
+            const bool live = i < nrow;
+            const float aji = live ? AP[apidx(r0 + i, lane)] : 0.f;
             float delta = 0.f;
-            if (lane == i) {
-                float ri = rj - ajj * fj;
+            if (live && lj == i) {
+                const float ri = rj - ajj * fj;
                 float fn = -ri * inv;
                 fn = fn > 0.f ? fn : 0.f;
                 delta = fn - fj;
                 fj = fn;
             }
-            delta = __shfl_sync(FULLMASK, delta, i);
+            delta = __shfl_sync(FULLMASK, delta, live ? r0 + i : lane);
             rj += aji * delta;
         }
     }
-    float* F = fr + L::FF;
-    if (lane < nefc) F[lane] = fj;
+    float* F = cw + CL::FF;
+    if (lane < nefc_all) F[lane] = fj;
     __syncwarp();
     PROF_MARK(P_PGS);
-    // qacc = qacc_smooth + sum_c sum_a fb_c[a] m_{c,a}  (env_qacc.cuh:199-211)
-    for (int d = lane; d < NV; d += 32) {
+    // qacc = qacc_smooth + sum_c sum_a fb_c[a] m_{c,a}, per world  (env_qacc.cuh:199-211)
+    for (int it = lane; it < B.nw * NV; it += 32) {
+        const int x = it / NV, d = it % NV;
+        float* qacc = grp + B.wid[x] * WFLOATS + WL::QACC;
         float dq = 0.f;
-        for (int c = 0; c < ncon; ++c) {
-            float f0 = F[4 * c], f1 = F[4 * c + 1], f2 = F[4 * c + 2], f3 = F[4 * c + 3];
-            float fb0 = f0 + f1 + f2 + f3, fb1 = f0 - f1, fb2 = f2 - f3;
-            const float* mc = MM + (1 + 3 * c) * MSTR;
+        for (int gc = B.coff[x]; gc < B.coff[x + 1]; ++gc) {
+            const float f0 = F[4 * gc], f1 = F[4 * gc + 1], f2 = F[4 * gc + 2], f3 = F[4 * gc + 3];
+            const float fb0 = f0 + f1 + f2 + f3, fb1 = f0 - f1, fb2 = f2 - f3;
+            const float* mc = MM + 3 * gc * MSTR;
             dq += fb0 * mc[d] + fb1 * mc[MSTR + d] + fb2 * mc[2 * MSTR + d];
         }
-        qacc[d] = MM[d] + dq;
+        qacc[d] = qacc[d] + dq;
     }
     __syncwarp();
     PROF_MARK(P_DQ);
-    return ncon;
+}
+
+// Full per-substep generalised acceleration for the GW worlds of the warp (qp, qv, tau
+// filled in each frame).  env_qacc.cuh:27-212.  qacc -> each frame's QACC; per-world
+// outputs for k_qacc through the optional arrays.
+__device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
+                           float* const* f_out, int* ncon_out, float* const* qs_out = nullptr) {
+    group_smooth(grp, T, lane, opt.bdt, bias_out);
+    PROF_BEGIN();
+    if (qs_out)
+        for (int it = lane; it < GW * NV; it += 32) {
+            const int w = it / NV, d = it % NV;
+            if (qs_out[w]) qs_out[w][d] = grp[w * WFLOATS + WL::QACC + d];
+        }
+    group_detect(grp, T, lane);
+    PROF_MARK(P_DETECT);
+    int ncon[GW];
+#pragma unroll
+    for (int w = 0; w < GW; ++w) {
+        ncon[w] = reinterpret_cast<const int*>(grp + w * WFLOATS + WL::MISC)[0];
+        if (ncon_out) ncon_out[w] = ncon[w];
+        if (f_out && f_out[w] && ncon[w] == 0) f_out[w][lane] = 0.f;
+    }
+    // greedy batches in slot order, at most MAXCON contacts each
+    Batch B;
+    B.nw = 0;
+    B.coff[0] = 0;
+#pragma unroll
+    for (int w = 0; w <= GW; ++w) {
+        const bool flush = (w == GW) ? B.nw > 0 : (ncon[w] > 0 && B.coff[B.nw] + ncon[w] > MAXCON);
+        if (flush) {
+            batch_contact(grp, cw, T, lane, opt, B);
+            if (f_out)
+                for (int x = 0; x < B.nw; ++x)
+                    if (f_out[B.wid[x]]) {
+                        const int n4 = 4 * (B.coff[x + 1] - B.coff[x]);
+                        f_out[B.wid[x]][lane] = lane < n4 ? cw[CL::FF + 4 * B.coff[x] + lane] : 0.f;
+                    }
+            B.nw = 0;
+        }
+        if (w < GW && ncon[w] > 0) {
+            B.wid[B.nw] = w;
+            B.coff[B.nw + 1] = B.coff[B.nw] + ncon[w];
+            ++B.nw;
+        }
+    }
 }
 
 // ------------------------------------------------------------------ integration
-// qvel += dt qacc (non-finite -> 0, clamp +-50), then the semi-implicit position update
-// with the base quaternion exponential.  g1_env.cu:154-162, dynamics.cuh:333-355
-__device__ void warp_integrate(float* fr, const G1Tables& T, int lane, bool guard) {
-    using L = FrameLayout;
-    float *qp = fr + L::QP, *qv = fr + L::QV;
-    const float* qacc = fr + L::QACC;
+// qvel += dt qacc (non-finite -> 0, clamp +-50), then the semi-implicit position update with
+// the base quaternion exponential, for the GW worlds.  g1_env.cu:154-162, dynamics.cuh:333-355
+__device__ void group_integrate(float* grp, const G1Tables& T, int lane, bool guard) {
     const float dt = G1M_DT;
-    for (int d = lane; d < NV; d += 32) {
-        float v = qv[d] + dt * qacc[d];
+    for (int it = lane; it < GW * NV; it += 32) {
+        const int w = it / NV, d = it % NV;
+        float* fr = grp + w * WFLOATS;
+        float v = fr[WL::QV + d] + dt * fr[WL::QACC + d];
         if (guard) {
             if (!isfinite(v)) v = 0.f;
             if (v > 50.f) v = 50.f; else if (v < -50.f) v = -50.f;
         }
-        qv[d] = v;
+        fr[WL::QV + d] = v;
     }
     __syncwarp();
-    for (int j = lane; j < NJ; j += 32) {
-        int qa = T.jnt_qposadr[j], da = T.jnt_dofadr[j];
+    for (int it = lane; it < GW * NJ; it += 32) {
+        const int w = it / NJ, j = it % NJ;
+        float* fr = grp + w * WFLOATS;
+        float *qp = fr + WL::QP;
+        const float* qv = fr + WL::QV;
+        const int qa = T.jnt_qposadr[j], da = T.jnt_dofadr[j];
         if (T.jnt_type[j] == 3) {
             qp[qa] += dt * qv[da];
         } else {
             qp[qa] += dt * qv[da]; qp[qa + 1] += dt * qv[da + 1]; qp[qa + 2] += dt * qv[da + 2];
-            V3 v = {qv[da + 3] * dt, qv[da + 4] * dt, qv[da + 5] * dt};
-            float ang = sqrtf(v.x * v.x + v.y * v.y + v.z * v.z);
+            const V3 v = {qv[da + 3] * dt, qv[da + 4] * dt, qv[da + 5] * dt};
+            const float ang = sqrtf(v.x * v.x + v.y * v.y + v.z * v.z);
             Q4 dq;
             if (ang < 1e-9f) dq = {1.f, 0.5f * v.x, 0.5f * v.y, 0.5f * v.z};
             else {
-                float s, c;
-                sincosf(0.5f * ang, &s, &c);
-                s = s / ang;
-                dq = {c, v.x * s, v.y * s, v.z * s};
+                float sn, cs;
+                sincosf(0.5f * ang, &sn, &cs);
+                sn = sn / ang;
+                dq = {cs, v.x * sn, v.y * sn, v.z * sn};
             }
-            Q4 qn = qnormalize(qmul(ld4(qp + qa + 3), dq));
-            st4(qp + qa + 3, qn);
+            st4(qp + qa + 3, qnormalize(qmul(ld4(qp + qa + 3), dq)));
         }
     }
     __syncwarp();

@@ -31,6 +31,7 @@
 #define G1_NRHS (1 + 3 * G1_MAXCON)
 #define G1_MAXCHAIN 6
 #define G1_MAXBRANCH 2
+#define G1_MAXXSLOT 4
 
 struct alignas(16) G1Tables {
     float body_pos[G1_NB * 3], body_quat[G1_NB * 4], body_ipos[G1_NB * 3], body_iquat[G1_NB * 4];
@@ -64,6 +65,8 @@ struct alignas(16) G1Tables {
     int chain_body[G1_MAXCHAIN][G1_NB];
     int branch_slot[G1_NB];  // bodies other than the base with >1 child: hand-off slot, else -1
     int head_chain[G1_NB];   // chain whose head is this body, else -1
+    int xslot[G1_NB];        // pelvis and foot bodies: slot of their kept frame, else -1
+    int nxslot;
 };
 
 #ifndef __CUDACC_RTC__
@@ -211,6 +214,11 @@ static inline void g1_build_tables(G1Tables* T) {
             if (nc > 1 && nslot < G1_MAXBRANCH) T->branch_slot[b] = nslot++;
         }
     }
+    for (int b = 0; b < G1_NB; ++b) T->xslot[b] = -1;
+    T->xslot[1] = 0;
+    T->nxslot = 1;
+    for (int s = 0; s < G1_NFOOT_; ++s)
+        if (T->xslot[G1M_FOOT_BODY[s]] < 0) T->xslot[G1M_FOOT_BODY[s]] = T->nxslot++;
     for (int s = 0; s < G1_NFOOT_; ++s) {
         int k = 0;
         for (int b = G1M_FOOT_BODY[s]; b >= 1; b = G1M_BODY_PARENT[b])

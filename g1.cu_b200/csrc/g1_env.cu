@@ -107,6 +107,7 @@ struct Params {
     float *obs_out, *rew_out, *done_out;
     int* ncon_hist;  // [MAXCON+1] contact-count histogram (substeps), may be null
     int lockstep;    // warps of a CTA walk their worlds in lockstep (named barrier per substep)
+    int* ncon_last;  // [N] contact count of each world's last substep (load balancing)
 };
 
 // ------------------------------------------------------------------ observations
@@ -234,6 +235,7 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
         if (lane < XSTR - OBS_DIM) X[w * XSTR + OBS_DIM + lane] = 0.f;
     }
     __syncthreads();
+    PROF_BEGIN();
     // hidden layers
     const float* wp = P.WT;
     const float* in = X;
@@ -252,6 +254,7 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
     cta_dense(wp, 32, wp + (size_t)nin * 32, nin, 30, in, istr, HD, 32, nbw, -1, WTILE);
     const float* lsp = wp + (size_t)nin * 32 + 32;
     __syncthreads();
+    PROF_MARK(P_MLP);
     // sampling: one thread per world, actions in index order (g1_env.cu:308-314)
     if (threadIdx.x < nbw) {
         const int w = threadIdx.x, gw = wbeg + w;
@@ -276,33 +279,35 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
         }
     }
     __syncthreads();
+    PROF_MARK(P_SAMPLE);
 }
 
 // ------------------------------------------------------------------ physics phase
 // Named barrier that keeps the CTA's warps on the same substep (so they fetch the same code).
 __device__ __forceinline__ void substep_barrier() { asm volatile("bar.sync 1, %0;" ::"r"(NTHREADS) : "memory"); }
 
-// One control step of GW worlds (global ids wg0 .. wg0+nvalid-1; the remaining slots carry a
+// One control step of GW worlds (global ids wid[0 .. nvalid-1]; the remaining slots carry a
 // stand pose and are not written back) by one warp: PD targets, S substeps, reward, done,
-// auto-reset.  env_advance, g1_env.cu:118-212.  `acts`: actions of world wg0 (row-major
-// [.,29], null = zero action).
-__device__ void group_control_step(const Params& P, const G1Tables& T, float* grp, float* cw, int wg0, int nvalid,
-                                   const float* acts, uint64_t tick, float* r_out, float* d_out) {
+// auto-reset.  env_advance, g1_env.cu:118-212.  `acts_base`: actions indexed by global world
+// id (row-major [N,29]; null = zero action).
+__device__ void group_control_step(const Params& P, const G1Tables& T, float* grp, float* cw, const int* wid, int nvalid,
+                                   const float* acts_base, uint64_t tick, float* r_out, float* d_out) {
     const int lane = threadIdx.x & 31;
+    // slot w < nvalid holds world wid[w]; its actions are acts_base[wid[w]] (null = zero)
     // load state
     for (int it = lane; it < GW * NQ; it += 32) {
         const int w = it / NQ, i = it % NQ;
-        grp[w * WFLOATS + WL::QP + i] = w < nvalid ? P.qp[(size_t)(wg0 + w) * NQ + i] : T.qpos_stand[i];
+        grp[w * WFLOATS + WL::QP + i] = w < nvalid ? P.qp[(size_t)wid[w] * NQ + i] : T.qpos_stand[i];
     }
     for (int it = lane; it < GW * 36; it += 32) {
         const int w = it / 36, i = it % 36;
         float* fr = grp + w * WFLOATS;
-        fr[WL::QV + i] = (w < nvalid && i < NV) ? P.qv[(size_t)(wg0 + w) * NV + i] : 0.f;
+        fr[WL::QV + i] = (w < nvalid && i < NV) ? P.qv[(size_t)wid[w] * NV + i] : 0.f;
         fr[WL::TAU + i] = 0.f;
     }
     for (int it = lane; it < GW * ACT_DIM; it += 32) {
         const int w = it / ACT_DIM, i = it % ACT_DIM;
-        const float a = (acts && w < nvalid) ? acts[(size_t)w * ACT_DIM + i] : 0.f;
+        const float a = (acts_base && w < nvalid) ? acts_base[(size_t)wid[w] * ACT_DIM + i] : 0.f;
         float t = T.target0[i] + ACT_SCALE * a;
         if (t < T.ctrl_lo[i]) t = T.ctrl_lo[i];
         if (t > T.ctrl_hi[i]) t = T.ctrl_hi[i];
@@ -340,6 +345,12 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
         group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon);
         if (P.ncon_hist && lane == 0)
             for (int w = 0; w < nvalid; ++w) atomicAdd(&P.ncon_hist[ncon[w]], 1);
+        if (s == P.S - 1 && P.ncon_last && lane < nvalid) {
+            int nc = 0;
+#pragma unroll
+            for (int w = 0; w < GW; ++w) nc = (w == lane) ? ncon[w] : nc;
+            P.ncon_last[wid[lane]] = nc;
+        }
         {
             PROF_BEGIN();
             group_integrate(grp, T, lane, true);
@@ -350,7 +361,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
     // reward / termination per world (g1_env.cu:164-197), lane w
     int d_flag = 0;
     if (lane < nvalid) {
-        const int w = lane, gw = wg0 + w;
+        const int w = lane, gw = wid[w];
         const float* fr = grp + w * WFLOATS;
         const float* qp = fr + WL::QP;
         const float* qv = fr + WL::QV;
@@ -368,7 +379,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
         const float r_h = -0.5f * fabsf(height - 0.78f);
         float act_pen = 0.f;
         for (int i = 0; i < ACT_DIM; ++i) {
-            const float da = (acts ? acts[(size_t)w * ACT_DIM + i] : 0.f) - P.pa[(size_t)gw * NU + i];
+            const float da = (acts_base ? acts_base[(size_t)gw * ACT_DIM + i] : 0.f) - P.pa[(size_t)gw * NU + i];
             act_pen += da * da;
         }
         if (act_pen > 10.f) act_pen = 10.f;
@@ -392,23 +403,23 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
     for (int it = lane; it < GW * ACT_DIM; it += 32) {
         const int w = it / ACT_DIM, i = it % ACT_DIM;
         if (w >= nvalid) continue;
-        const int gw = wg0 + w;
+        const int gw = wid[w];
         if ((dmask >> w) & 1u) {
             const uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)gw, tick, RNG_AUTORESET, (uint32_t)i);
             grp[w * WFLOATS + WL::QP + T.act_qadr[i]] += 0.05f * (u01_open(rb.x) * 2.f - 1.f);
             P.pa[(size_t)gw * NU + i] = 0.f;
         } else {
-            P.pa[(size_t)gw * NU + i] = acts ? acts[(size_t)w * ACT_DIM + i] : 0.f;
+            P.pa[(size_t)gw * NU + i] = acts_base ? acts_base[(size_t)gw * ACT_DIM + i] : 0.f;
         }
     }
     __syncwarp();
     for (int it = lane; it < GW * NQ; it += 32) {
         const int w = it / NQ, i = it % NQ;
-        if (w < nvalid) P.qp[(size_t)(wg0 + w) * NQ + i] = grp[w * WFLOATS + WL::QP + i];
+        if (w < nvalid) P.qp[(size_t)wid[w] * NQ + i] = grp[w * WFLOATS + WL::QP + i];
     }
     for (int it = lane; it < GW * NV; it += 32) {
         const int w = it / NV, i = it % NV;
-        if (w < nvalid) P.qv[(size_t)(wg0 + w) * NV + i] = ((dmask >> w) & 1u) ? 0.f : grp[w * WFLOATS + WL::QV + i];
+        if (w < nvalid) P.qv[(size_t)wid[w] * NV + i] = ((dmask >> w) & 1u) ? 0.f : grp[w * WFLOATS + WL::QV + i];
     }
     __syncwarp();
 }
@@ -421,7 +432,7 @@ __host__ __device__ inline SmemPlan smem_plan() {
     SmemPlan p;
     p.tab_floats = ((int)((sizeof(G1Tables) + 15) / 16)) * 4;
     p.group_floats = GROUP_FLOATS + GW * 36;  // + per-world damping rows (k_qacc)
-    p.total_bytes = (p.tab_floats + NWARPS * p.group_floats + 4) * 4;
+    p.total_bytes = (p.tab_floats + NWARPS * p.group_floats + 4 + MAX_WB) * 4;
     return p;
 }
 static_assert(MAX_WB * XSTR + 2 * MAX_WB * 260 + KT * OC <= NWARPS * GROUP_FLOATS, "MLP activations must fit in the frames");
@@ -449,6 +460,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
     if (nbw <= 0) return;
     const int nsteps = P.mode == MODE_ROLLOUT ? P.H : (P.mode == MODE_PHYS ? P.K : 1);
     const int nrounds = (nbw + GW * NWARPS - 1) / (GW * NWARPS);
+    int* perm = reinterpret_cast<int*>(frames + NWARPS * plan.group_floats + 4);
     for (int t = 0; t < nsteps; ++t) {
         const uint64_t tick = P.tick0 + (uint64_t)t;
         if (P.mode == MODE_ROLLOUT) {
@@ -457,35 +469,65 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
             PROF_MARK(P_POLICY);
         }
         __syncthreads();
-        // physics: warp takes world groups warp, warp + NWARPS, ... of the block; a warp with no
-        // group in a round still passes the substep barriers
+        // physics.  Worlds are dealt into groups of GW: sorted by their last contact count
+        // (descending, stable) and dealt in snake order over the groups, so every warp gets a
+        // similar contact load.  Warp takes groups warp, warp + NWARPS, ...; a warp with no
+        // group in a round still passes the substep barriers.
+        const int ngroups = (nbw + GW - 1) / GW;
+        if (warp == 0) {
+            int v0 = -1, v1 = -1;  // this lane's two worlds (nbw <= 64)
+            if (lane < nbw) v0 = P.ncon_last ? P.ncon_last[wbeg + lane] : 0;
+            if (lane + 32 < nbw) v1 = P.ncon_last ? P.ncon_last[wbeg + lane + 32] : 0;
+            int base = 0;
+            for (int v = MAXCON; v >= 0; --v) {
+                const unsigned m0 = __ballot_sync(FULLMASK, v0 == v), m1 = __ballot_sync(FULLMASK, v1 == v);
+                const unsigned below = (1u << lane) - 1u;
+                if (v0 == v) perm[base + __popc(m0 & below)] = lane;
+                if (v1 == v) perm[base + __popc(m0) + __popc(m1 & below)] = lane + 32;
+                base += __popc(m0) + __popc(m1);
+            }
+        }
+        __syncthreads();
         for (int round = 0; round < nrounds; ++round) {
-            const int w0 = (warp + round * NWARPS) * GW;
-            const int nvalid = max(0, min(GW, nbw - w0));
+            const int g = warp + round * NWARPS;
+            int wid[GW];
+            int nvalid = 0;
+#pragma unroll
+            for (int sl = 0; sl < GW; ++sl) {
+                const int pidx = sl * ngroups + ((sl & 1) ? ngroups - 1 - g : g);
+                wid[sl] = wbeg;
+                if (g < ngroups && pidx < nbw) wid[nvalid++] = wbeg + perm[pidx];
+            }
             if (nvalid == 0) {
                 if (P.lockstep)
                     for (int s = 0; s < P.S; ++s) substep_barrier();
                 continue;
             }
-            const int wg0 = wbeg + w0;
-            const float* acts = P.mode == MODE_ROLLOUT ? P.A + ((size_t)t * P.N + wg0) * ACT_DIM
-                              : (P.mode == MODE_STEP ? P.act_in + (size_t)wg0 * ACT_DIM : nullptr);
+            const float* acts = P.mode == MODE_ROLLOUT ? P.A + (size_t)t * P.N * ACT_DIM
+                              : (P.mode == MODE_STEP ? P.act_in : nullptr);
             float r[GW], d[GW];
-            group_control_step(P, T, grp, cw, wg0, nvalid, acts, tick, r, d);
+            group_control_step(P, T, grp, cw, wid, nvalid, acts, tick, r, d);
+            int my_w = 0;
+            float my_r = 0.f, my_d = 0.f;
+#pragma unroll
+            for (int sl = 0; sl < GW; ++sl)
+                if (sl == lane) { my_w = wid[sl]; my_r = r[sl]; my_d = d[sl]; }
             if (lane < nvalid) {
-                const int gw = wg0 + lane;
                 if (P.mode == MODE_ROLLOUT) {
-                    P.R[(size_t)t * P.N + gw] = r[lane];
-                    P.D[(size_t)t * P.N + gw] = d[lane];
+                    P.R[(size_t)t * P.N + my_w] = my_r;
+                    P.D[(size_t)t * P.N + my_w] = my_d;
                 } else if (P.mode == MODE_STEP) {
-                    P.rew_out[gw] = r[lane];
-                    P.done_out[gw] = d[lane];
+                    P.rew_out[my_w] = my_r;
+                    P.done_out[my_w] = my_d;
                 }
             }
             if (P.mode == MODE_STEP) {  // k_step's obs after the step (g1_env.cu:265-266)
                 __syncwarp();
                 for (int it = lane; it < nvalid * OBS_DIM; it += 32) {
-                    const int w = it / OBS_DIM, i = it % OBS_DIM, gw = wg0 + w;
+                    const int sl = it / OBS_DIM, i = it % OBS_DIM;
+                    int gw = wid[0];
+#pragma unroll
+                    for (int q = 1; q < GW; ++q) gw = (q == sl) ? wid[q] : gw;
                     P.obs_out[(size_t)gw * OBS_DIM + i] =
                         obs_elem(i, P.qp + (size_t)gw * NQ, P.qv + (size_t)gw * NV, P.pa + (size_t)gw * NU, T);
                 }
@@ -626,6 +668,7 @@ struct EnvState {
     int nh, hid[MAX_HIDDEN], act;
     int sm_count;
     int* ncon_hist;
+    int* ncon_last;
     cudaStream_t stream;                // 0 = legacy default stream (the reference's)
 };
 
@@ -653,6 +696,7 @@ static Params base_params(EnvState* E) {
     P.nh = E->nh; P.act = E->act;
     for (int i = 0; i < MAX_HIDDEN; ++i) P.hid[i] = E->hid[i];
     P.ncon_hist = E->ncon_hist;
+    P.ncon_last = E->ncon_last;
     P.lockstep = getenv("G1_LOCKSTEP") ? atoi(getenv("G1_LOCKSTEP")) : 1;
     // worlds per CTA: spread over all SMs, at most MAX_WB (then CTAs run in waves)
     int wb = (E->N + E->sm_count - 1) / E->sm_count;
@@ -709,11 +753,12 @@ void* g1_env_create_ex(int N, int substeps, int pgs_iters, unsigned long seed, i
               cudaMalloc(&E->pa, (size_t)N * NU * 4) == cudaSuccess && cudaMalloc(&E->steps, (size_t)N * 4) == cudaSuccess &&
               cudaMalloc(&E->dact, (size_t)N * ACT_DIM * 4) == cudaSuccess &&
               cudaMalloc(&E->dobs, (size_t)N * OBS_DIM * 4) == cudaSuccess && cudaMalloc(&E->drew, (size_t)N * 4) == cudaSuccess &&
-              cudaMalloc(&E->ddone, (size_t)N * 4) == cudaSuccess;
+              cudaMalloc(&E->ddone, (size_t)N * 4) == cudaSuccess && cudaMalloc(&E->ncon_last, (size_t)N * 4) == cudaSuccess &&
+              cudaMemset(E->ncon_last, 0, (size_t)N * 4) == cudaSuccess;
     if (!ok) {
         set_error(2, "g1_env_create", "cudaMalloc failed");
         cudaFree(E->qp); cudaFree(E->qv); cudaFree(E->pa); cudaFree(E->steps);
-        cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone);
+        cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone); cudaFree(E->ncon_last);
         delete E;
         return nullptr;
     }
@@ -735,7 +780,7 @@ void g1_env_destroy(void* h) {  // g1_env.cu:469-474
     if (!E) return;
     cudaFree(E->qp); cudaFree(E->qv); cudaFree(E->pa); cudaFree(E->steps);
     cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone);
-    cudaFree(E->WT); cudaFree(E->ncon_hist);
+    cudaFree(E->WT); cudaFree(E->ncon_hist); cudaFree(E->ncon_last);
     delete E;
 }
 

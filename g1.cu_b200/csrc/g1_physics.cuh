@@ -193,7 +193,7 @@ __device__ unsigned long long g_prof[16];
 #define PROF_BEGIN()
 #define PROF_MARK(i) do { } while (0)
 #endif
-enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_NPHASE };
+enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_NPHASE };
 
 // pyramid coefficients d_k = DC[k] of the 3-basis (env_qacc.cuh:98-100,154-155)
 __device__ __forceinline__ float dcoef(int k, int a) {
@@ -489,24 +489,33 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
     }
     __syncwarp();
     if (w < GW && cl == 0) {
-        float* Dm = L6;  // in-place Cholesky (aba_factor.cuh:103-107); one lane per world
-#pragma unroll 1
+        // 6x6 Cholesky of Dm and the base solve in registers (aba_factor.cuh:103-107,
+        // 148-152); one lane per world
+        float Dm[36];
+#pragma unroll
+        for (int k = 0; k < 36; ++k) Dm[k] = L6[k];
+#pragma unroll
         for (int i = 0; i < 6; ++i)
-#pragma unroll 1
+#pragma unroll
             for (int j = 0; j <= i; ++j) {
                 float acc = Dm[i * 6 + j];
+#pragma unroll
                 for (int k = 0; k < j; ++k) acc -= Dm[i * 6 + k] * Dm[j * 6 + k];
                 if (i == j) Dm[i * 6 + i] = sqrtf(acc); else Dm[i * 6 + j] = acc / Dm[j * 6 + j];
             }
-#pragma unroll 1
+#pragma unroll
+        for (int k = 0; k < 36; ++k) L6[k] = Dm[k];
+#pragma unroll
         for (int i = 0; i < 6; ++i) {
             float acc = q6[i];
+#pragma unroll
             for (int k = 0; k < i; ++k) acc -= Dm[i * 6 + k] * q6[k];
             q6[i] = acc / Dm[i * 6 + i];
         }
-#pragma unroll 1
+#pragma unroll
         for (int i = 5; i >= 0; --i) {
             float acc = q6[i];
+#pragma unroll
             for (int k = i + 1; k < 6; ++k) acc -= Dm[k * 6 + i] * q6[k];
             q6[i] = acc / Dm[i * 6 + i];
         }
@@ -564,29 +573,25 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
 // its contribution in hand[chain]; a body adds its children in descending child index.
 // u_b = x_d - S_d.pA_b parks in xy[d] between the sweeps; root->leaf a branch body leaves
 // its acceleration in fwd[slot].  `scratch`: SOLVE_SCRATCH floats of this lane.
-constexpr int MAXCL = 12;  // longest chain the unrolled solve handles
 __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, float* xy, float* scratch) {
     const float *S = fr + WL::S, *FU = fr + WL::FU, *FINVD = fr + WL::FINVD, *L6 = fr + WL::FL6;
     float* hand = scratch;
     float* fwd = scratch + 6 * 4;
-    // leaf -> root, chains last-to-first
+    // leaf -> root, chains last-to-first; the next body's index is fetched one body ahead
     for (int c = T.nchain - 1; c >= 0; --c) {
         const int len = T.chain_len[c];
-        int bl[MAXCL];
-#pragma unroll
-        for (int k = 0; k < MAXCL; ++k) bl[k] = k < len ? T.chain_body[c][k] : 0;
         float pa[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = MAXCL - 1; k >= 0; --k) {
-            if (k >= len) continue;
-            const int b = bl[k], d = T.dofadr[b];
+        int b = T.chain_body[c][len - 1], prev = -1;
+        for (int k = len - 1; k >= 0; --k) {
+            const int bn = k > 0 ? T.chain_body[c][k - 1] : 0;
+            const int d = T.dofadr[b];
             float acc[6];
             if (T.branch_slot[b] >= 0) {  // branch body: children in descending index
 #pragma unroll
                 for (int i = 0; i < 6; ++i) acc[i] = 0.f;
                 for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
                     const int ch = T.child_list[q];
-                    if (k + 1 < len && ch == bl[(k + 1 < MAXCL) ? k + 1 : k]) {
+                    if (ch == prev) {
 #pragma unroll
                         for (int i = 0; i < 6; ++i) acc[i] += pa[i];
                     } else {
@@ -595,7 +600,7 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
                         for (int i = 0; i < 6; ++i) acc[i] += src[i];
                     }
                 }
-            } else {  // one child (the next body of the chain) or a leaf
+            } else {  // one child (the previous body of the walk) or a leaf
 #pragma unroll
                 for (int i = 0; i < 6; ++i) acc[i] = pa[i];
             }
@@ -607,6 +612,8 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
             const float* U = FU + 6 * b;
 #pragma unroll
             for (int i = 0; i < 6; ++i) pa[i] = acc[i] + U[i] * ud;
+            prev = b;
+            b = bn;
         }
 #pragma unroll
         for (int i = 0; i < 6; ++i) hand[6 * c + i] = pa[i];
@@ -623,17 +630,24 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
         const float* sd = S + 6 * k;
         q6[k] = xy[k] - (((((0.f + sd[0] * pa1[0]) + sd[1] * pa1[1]) + sd[2] * pa1[2]) + sd[3] * pa1[3]) + sd[4] * pa1[4] + sd[5] * pa1[5]);
     }
-#pragma unroll 1
+    float Lr[21];  // lower triangle of the base Cholesky factor
+#pragma unroll
+    for (int i = 0; i < 6; ++i)
+#pragma unroll
+        for (int k = 0; k <= i; ++k) Lr[i * (i + 1) / 2 + k] = L6[i * 6 + k];
+#pragma unroll
     for (int i = 0; i < 6; ++i) {
         float acc = q6[i];
-        for (int k = 0; k < i; ++k) acc -= L6[i * 6 + k] * q6[k];
-        q6[i] = acc / L6[i * 6 + i];
+#pragma unroll
+        for (int k = 0; k < i; ++k) acc -= Lr[i * (i + 1) / 2 + k] * q6[k];
+        q6[i] = acc / Lr[i * (i + 1) / 2 + i];
     }
-#pragma unroll 1
+#pragma unroll
     for (int i = 5; i >= 0; --i) {
         float acc = q6[i];
-        for (int k = i + 1; k < 6; ++k) acc -= L6[k * 6 + i] * q6[k];
-        q6[i] = acc / L6[i * 6 + i];
+#pragma unroll
+        for (int k = i + 1; k < 6; ++k) acc -= Lr[k * (k + 1) / 2 + i] * q6[k];
+        q6[i] = acc / Lr[i * (i + 1) / 2 + i];
     }
     float a1[6];
 #pragma unroll
@@ -648,10 +662,8 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
     // root -> leaf, chains first-to-last
     for (int c = 0; c < T.nchain; ++c) {
         const int len = T.chain_len[c];
-        int bl[MAXCL];
-#pragma unroll
-        for (int k = 0; k < MAXCL; ++k) bl[k] = k < len ? T.chain_body[c][k] : 0;
-        const int par = T.parent[bl[0]];
+        int b = T.chain_body[c][0];
+        const int par = T.parent[b];
         float a[6];
         if (par == 1) {
 #pragma unroll
@@ -661,10 +673,9 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
 #pragma unroll
             for (int i = 0; i < 6; ++i) a[i] = src[i];
         }
-#pragma unroll
-        for (int k = 0; k < MAXCL; ++k) {
-            if (k >= len) continue;
-            const int b = bl[k], d = T.dofadr[b];
+        for (int k = 0; k < len; ++k) {
+            const int bn = k + 1 < len ? T.chain_body[c][k + 1] : 0;
+            const int d = T.dofadr[b];
             const float* U = FU + 6 * b;
             const float s2 = ((((0.f + U[0] * a[0]) + U[1] * a[1]) + U[2] * a[2]) + U[3] * a[3]) + U[4] * a[4] + U[5] * a[5];
             const float qdd = (xy[d] - s2) * FINVD[b];
@@ -677,6 +688,7 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
 #pragma unroll
                 for (int i = 0; i < 6; ++i) dst[i] = a[i];
             }
+            b = bn;
         }
     }
 }
@@ -745,7 +757,7 @@ struct Batch {
 // by side; the Delassus matrix is block diagonal over worlds and each world's PGS sweeps
 // its own rows in order, all worlds in the same pass.  f -> cw[FF] (world x's rows start at
 // 4*coff[x]).
-__device__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, const Batch& B) {
+__device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, const Batch& B) {
     float* MM = cw + CL::MM;
     float* EB = cw + CL::EB;
     const int nc = B.coff[B.nw], nb = 3 * nc, nefc_all = 4 * nc;
@@ -938,7 +950,7 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
     Batch B;
     B.nw = 0;
     B.coff[0] = 0;
-#pragma unroll
+#pragma unroll 1
     for (int w = 0; w <= GW; ++w) {
         const bool flush = (w == GW) ? B.nw > 0 : (ncon[w] > 0 && B.coff[B.nw] + ncon[w] > MAXCON);
         if (flush) {

@@ -722,6 +722,31 @@ static size_t policy_floats(int nh, const int* hid) {
     return n + (size_t)nin * 32 + 64;
 }
 
+// ------------------------------------------------------------------ allocation-free rollout
+// g1_rollout repacks the policy weights into a buffer the env allocates on first use (and
+// reallocates when the policy grows).  g1_rollout_noalloc keeps that repacked copy in this
+// fixed device array instead, so it never allocates.  Every GPU that loads the library holds
+// the array until the process exits.  All calls share it: each call rewrites the part it
+// uses before reading it, and calls that overlap on the GPU (other streams, other threads)
+// race on it.
+#define G1_NOALLOC_WT_FLOATS (128 * 1024)  // 512 KiB: fits the reference's 100-256-256 policy (99,904 floats)
+static __device__ __align__(256) float g_noalloc_wt[G1_NOALLOC_WT_FLOATS];
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[64];  // device address of g_noalloc_wt, per device ordinal
+
+// Device address of the static weight area on the current device, looked up once per
+// device (cudaGetSymbolAddress; the host-side name g_noalloc_wt is not a device address).
+static float* noalloc_area(int dev) {
+    if (dev < 0 || dev >= 64) { set_error(-22, "g1_rollout_noalloc", "device ordinal out of range"); return nullptr; }
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        float* ptr = nullptr;
+        CKR(cudaGetSymbolAddress((void**)&ptr, g_noalloc_wt), nullptr);
+        g_noalloc_ptr[dev] = ptr;
+    }
+    return g_noalloc_ptr[dev];
+}
+
 extern "C" {
 
 const char* g1_env_last_error(void) {
@@ -854,6 +879,34 @@ void g1_rollout(void* h, int H, const float* W, const float* mean, const float* 
     Params P = base_params(E);
     P.mode = MODE_ROLLOUT; P.H = H;
     P.WT = E->WT; P.mean = mean; P.var = var;
+    P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
+    if (launch_g1(E, P)) E->tick += (uint64_t)H;
+}
+
+// Same as g1_rollout, but allocates nothing: the repacked policy weights go to the fixed
+// device area g_noalloc_wt (G1_NOALLOC_WT_FLOATS floats) instead of an env-owned buffer.
+// Rejects a policy whose repacked size exceeds that area.  The first call on a device looks
+// up the area's device address; make that first call before any stream capture.
+void g1_rollout_noalloc(void* h, int H, const float* W, const float* mean, const float* var, float* O, float* A,
+                        float* LP, float* V, float* R, float* D, float* Vlast) {
+    EnvState* E = (EnvState*)h;
+    if (H <= 0) return;
+    const size_t need = policy_floats(E->nh, E->hid);
+    if (need > (size_t)G1_NOALLOC_WT_FLOATS) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "policy needs %zu floats of repacked weights; the static area holds %d", need,
+                 G1_NOALLOC_WT_FLOATS);
+        set_error(-22, "g1_rollout_noalloc", msg);
+        return;
+    }
+    float* wt = noalloc_area(E->device);
+    if (!wt) return;
+    // k_repack writes all `need` floats of the area, so no clearing is needed
+    k_repack<<<120, 256, 0, E->stream>>>(W, wt, E->nh, E->hid[0], E->hid[1], E->hid[2], E->hid[3]);
+    CKR(cudaGetLastError(), );
+    Params P = base_params(E);
+    P.mode = MODE_ROLLOUT; P.H = H;
+    P.WT = wt; P.mean = mean; P.var = var;
     P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
     if (launch_g1(E, P)) E->tick += (uint64_t)H;
 }

@@ -32,6 +32,7 @@ SIGNATURES = {
     "g1_env_step": (None, [_vp, _fp, _fp, _fp, _fp]),
     "g1_env_step_device": (None, [_vp] + [_vp] * 4),
     "g1_rollout": (None, [_vp, ctypes.c_int] + [_vp] * 10),
+    "g1_rollout_noalloc": (None, [_vp, ctypes.c_int] + [_vp] * 10),
     "g1_env_bench_phys": (None, [_vp, ctypes.c_int]),
     "g1_env_phys_async": (None, [_vp, ctypes.c_int]),
     "g1_env_qpos": (None, [_vp, _fp]),
@@ -143,6 +144,13 @@ class G1Env:
         """g1_rollout on torch-owned device tensors (ppo_fused.py:101-102)."""
         _lib.g1_rollout(self.h, H, _dp(W), _dp(mean), _dp(var), _dp(O), _dp(A), _dp(LP), _dp(V), _dp(R), _dp(D),
                         _dp(Vlast))
+        _check()
+
+    def rollout_noalloc(self, H, W, mean, var, O, A, LP, V, R, D, Vlast):
+        """g1_rollout_noalloc: the same rollout without any device allocation (weights repacked
+        into the library's fixed device area)."""
+        _lib.g1_rollout_noalloc(self.h, H, _dp(W), _dp(mean), _dp(var), _dp(O), _dp(A), _dp(LP), _dp(V), _dp(R),
+                                _dp(D), _dp(Vlast))
         _check()
 
     def bench_phys(self, K):

@@ -52,6 +52,16 @@ void g1_env_step_device(void* h, const float* act, float* obs, float* rew, float
 void g1_rollout(void* h, int H, const float* W, const float* mean, const float* var, float* O, float* A,
                 float* LP, float* V, float* R, float* D, float* Vlast);
 
+/* extension, no counterpart in the reference: g1_rollout that allocates nothing, for callers
+ * that must not allocate device memory on their hot path (a host allocator that owns all
+ * device memory, a pre-reserved memory budget, or code running while a stream is captured).
+ * The repacked policy weights live in a fixed 512 KiB device area (131,072 floats) shared by
+ * all calls and all envs on a device: policies needing more are rejected (last error set),
+ * and calls that overlap on the GPU race on the area.  The first call on each device looks
+ * up the area's address; make it before any stream capture.  Arguments as g1_rollout. */
+void g1_rollout_noalloc(void* h, int H, const float* W, const float* mean, const float* var, float* O, float* A,
+                        float* LP, float* V, float* R, float* D, float* Vlast);
+
 /* replaces g1_env_bench_phys, g1_env.cu:385-389: K control steps with zero action, synchronous. */
 void g1_env_bench_phys(void* h, int K);
 

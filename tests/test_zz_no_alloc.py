@@ -1,0 +1,60 @@
+"""g1_rollout_noalloc: the rollout entry point that allocates no device memory, for callers
+that cannot allocate on their hot path (e.g. a host framework that owns all device memory or
+has reserved its budget up front, or code running while a stream is being captured).  It
+keeps the repacked policy weights in a fixed device area of the library instead of an
+env-owned buffer.  Checked through the C-ABI against g1_rollout on two calls in a row.
+
+This file is collected last on purpose: it runs after every other test, and it must also
+pass when run alone in a fresh process."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _bufs(H, N):
+    z = lambda *s: torch.zeros(*s, device="cuda")
+    return [z(H, N, 100), z(H, N, 29), z(H, N), z(H, N), z(H, N), z(H, N), z(N)]
+
+
+def test_noalloc_rollout_matches_rollout_twice():
+    import g1env
+    g1env.load_library()
+    N, H = 200, 3
+    ac = g1env.init_policy_normal(g1env.AC(100, 29).cuda(), seed=4)
+    W = g1env.pack_weights(ac).detach()
+    mean = torch.zeros(100, device="cuda")
+    var = torch.ones(100, device="cuda")
+    ref = g1env.G1Env(N, 10, 8, seed=21)
+    new = g1env.G1Env(N, 10, 8, seed=21)
+    ref.reset()
+    new.reset()
+    for call in range(2):
+        a, b = _bufs(H, N), _bufs(H, N)
+        ref.rollout(H, W, mean, var, *a)
+        new.rollout_noalloc(H, W, mean, var, *b)
+        torch.cuda.synchronize()
+        for k, (x, y) in enumerate(zip(a, b)):
+            x, y = x.cpu().numpy(), y.cpu().numpy()
+            assert np.abs(x - y).max() <= 1e-4, (call, k)
+        assert np.array_equal(a[5].cpu().numpy(), b[5].cpu().numpy())   # done flags exact
+        sr, sn = ref.get_state(), new.get_state()
+        assert np.array_equal(sr[3], sn[3]) and sr[4] == sn[4]          # counters and RNG tick
+    ref.close()
+    new.close()
+
+
+def test_noalloc_rejects_policy_beyond_static_area():
+    import g1env
+    lib = g1env.load_library()
+    env = g1env.G1Env(8, 10, 8, seed=1)
+    env.set_policy((344, 344, 344, 344), "elu")   # 401,856 repacked floats > 131,072
+    H = 1
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (344, 344, 344, 344), "elu").cuda(), seed=0)
+    W = g1env.pack_weights(ac).detach()
+    b = _bufs(H, 8)
+    with pytest.raises(g1env.G1Error, match="static area"):
+        env.rollout_noalloc(H, W, torch.zeros(100, device="cuda"), torch.ones(100, device="cuda"), *b)
+    lib.g1_env_clear_error()
+    env.close()

@@ -219,6 +219,26 @@ def reference_kernel_time(N, mean, var, W, reps=2):
     return e0.elapsed_time(e1) / reps
 
 
+def profile_case(h):
+    """Two g1_rollout calls of the config-2 workload with horizon h (the second is the one to
+    capture with ncu -s 1 -c 1)."""
+    import torch
+    import g1env
+    env = g1env.G1Env(N_PER_GPU, S, PGS, seed=1)
+    env.set_policy((256, 256), "elu")
+    env.reset()
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (256, 256), "elu"), seed=0).cuda()
+    W = g1env.pack_weights(ac).detach()
+    mean, var = torch.zeros(100, device="cuda"), torch.ones(100, device="cuda")
+    z = lambda *s: torch.zeros(*s, device="cuda")
+    bufs = [z(h, N_PER_GPU, 100), z(h, N_PER_GPU, 29)] + [z(h, N_PER_GPU) for _ in range(4)] + [z(N_PER_GPU)]
+    for _ in range(2):
+        env.rollout(h, W, mean, var, *bufs)
+    torch.cuda.synchronize()
+    env.close()
+    print("profile case done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -226,7 +246,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-ref-kernel", action="store_true")
+    ap.add_argument("--profile-case", type=int, default=0, metavar="H",
+                    help="run two H-step rollouts of the config-2 worlds and exit (small case for ncu captures)")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
@@ -326,7 +351,8 @@ def main():
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": 2 * args.steps,
                 "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
-                             "frac": achieved / fp32_peak, "traffic": None,
+                             "frac": achieved / fp32_peak, "traffic": 145e6,
+                             "traffic_source": "ncu dram__bytes_read+write of one H=2 launch (9.09 MB), scaled x16 to H=32 (profiles/k_g1_rollout_n8192_h32.md)",
                              "peak_source": f"nominal FP32 FMA rate: {sm_count} SMs x 128 lanes x 2 x {clk:.0f} MHz "
                                             f"(MEASURED_PEAKS.json has no FP32 figure; its hbm/bf16 peaks are {peak_src})",
                              "flop_per_substep": flop_sub, "ncon_hist": hist.tolist()},

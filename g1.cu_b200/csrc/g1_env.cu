@@ -131,8 +131,9 @@ __device__ __forceinline__ float obs_elem(int i, const float* qp, const float* q
 // weights are staged through shared memory in tiles of KT inputs x OC outputs (coalesced
 // loads, reused by every world of the block); a thread owns 2 outputs x 4 worlds of an
 // output chunk.  nin must be a multiple of 4 (inputs are read as float4).
-#define KT 32
+#define KT 64
 #define OC 64
+#define TILE_PER ((KT * OC + NTHREADS - 1) / NTHREADS)
 __device__ __noinline__ void cta_dense(const float* __restrict__ WT, int wstr, const float* __restrict__ bias, int nin, int nout,
                                        const float* in, int istr, float* out, int ostr, int nw, int act, float* wtile) {
     const int nwg = (nw + 3) >> 2;
@@ -150,14 +151,28 @@ __device__ __noinline__ void cta_dense(const float* __restrict__ WT, int wstr, c
 #pragma unroll
             for (int k = 0; k < 4; ++k) { acc[j][k][0] = b0; acc[j][k][1] = b1; }
         }
+        // weight tiles are fetched one tile ahead into registers, so the global loads of tile
+        // k+1 are in flight while tile k is multiplied
+        float pre[TILE_PER];
+        auto fetch = [&](int k0) {
+            const int kt = min(KT, nin - k0);
+#pragma unroll
+            for (int q = 0; q < TILE_PER; ++q) {
+                const int e = threadIdx.x + q * NTHREADS, kk = e / OC, oo = e % OC;
+                pre[q] = (e < KT * OC && kk < kt && oc0 + oo < nout) ? __ldg(WT + (size_t)(k0 + kk) * wstr + oc0 + oo) : 0.f;
+            }
+        };
+        fetch(0);
         for (int k0 = 0; k0 < nin; k0 += KT) {
             const int kt = min(KT, nin - k0);
             __syncthreads();  // previous tile consumed
-            for (int e = threadIdx.x; e < KT * OC; e += NTHREADS) {
-                const int kk = e / OC, oo = e % OC;
-                wtile[e] = (kk < kt && oc0 + oo < nout) ? __ldg(WT + (size_t)(k0 + kk) * wstr + oc0 + oo) : 0.f;
+#pragma unroll
+            for (int q = 0; q < TILE_PER; ++q) {
+                const int e = threadIdx.x + q * NTHREADS;
+                if (e < KT * OC) wtile[e] = pre[q];
             }
             __syncthreads();
+            if (k0 + KT < nin) fetch(k0 + KT);
 #pragma unroll
             for (int j = 0; j < MAXIT; ++j) {
                 const int it = threadIdx.x + j * NTHREADS;

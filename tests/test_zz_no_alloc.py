@@ -49,9 +49,9 @@ def test_noalloc_rejects_policy_beyond_static_area():
     import g1env
     lib = g1env.load_library()
     env = g1env.G1Env(8, 10, 8, seed=1)
-    env.set_policy((344, 344, 344, 344), "elu")   # 401,856 repacked floats > 131,072
+    env.set_policy((300, 300, 300, 300), "elu")   # 310,864 repacked floats > 131,072
     H = 1
-    ac = g1env.init_policy_normal(g1env.AC(100, 29, (344, 344, 344, 344), "elu").cuda(), seed=0)
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (300, 300, 300, 300), "elu").cuda(), seed=0)
     W = g1env.pack_weights(ac).detach()
     b = _bufs(H, 8)
     with pytest.raises(g1env.G1Error, match="static area"):

@@ -26,6 +26,7 @@
 #include <string>
 
 #include "g1_physics.cuh"
+#include "g1_mlp_tc.cuh"
 #include "../../include/g1env.h"
 
 using namespace g1;
@@ -737,6 +738,31 @@ static size_t policy_floats(int nh, const int* hid) {
     return n + (size_t)nin * 32 + 64;
 }
 
+// ------------------------------------------------------------------ tensor-core dense layer
+// out = act(X W^T + b) on tcgen05 (g1_mlp_tc.cuh); N tiles of BN = 256 (smaller for narrow
+// layers).  Asynchronous on `stream`; *err (device) is set if an MMA wait timed out.
+template <int BN>
+static cudaError_t launch_dense_tc(int M, int N, int K, const __nv_bfloat16* X, int ldx, const __nv_bfloat16* W,
+                                   const float* bias, int act, float* of, int ldo, __nv_bfloat16* ob, int ldob, int* err,
+                                   cudaStream_t stream) {
+    static bool attr = false;  // per process: the attribute is per function, set before first launch
+    const int smem = g1tc::dense_tc_smem<BN>();
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(g1tc::k_dense_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    dim3 grid((M + g1tc::TM - 1) / g1tc::TM, (N + BN - 1) / BN);
+    g1tc::k_dense_tc<BN><<<grid, g1tc::NTH, smem, stream>>>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err);
+    return cudaGetLastError();
+}
+static cudaError_t dense_tc(int M, int N, int K, const __nv_bfloat16* X, int ldx, const __nv_bfloat16* W, const float* bias,
+                            int act, float* of, int ldo, __nv_bfloat16* ob, int ldob, int* err, cudaStream_t stream) {
+    if (N <= 32) return launch_dense_tc<32>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+    if (N <= 64) return launch_dense_tc<64>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+    return launch_dense_tc<256>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+}
+
 // ------------------------------------------------------------------ allocation-free rollout
 // g1_rollout repacks the policy weights into a buffer the env allocates on first use (and
 // reallocates when the policy grows).  g1_rollout_noalloc keeps that repacked copy in this
@@ -1028,6 +1054,26 @@ int g1_prof_read(unsigned long long* out) {
     return 0;
 }
 #endif
+
+// extension: one dense layer out = act(X W^T + b) on the tensor cores (tcgen05, bf16 inputs,
+// fp32 accumulation).  DEVICE pointers: X [M][K] bf16 (row stride ldx), W [N][K] bf16, bias
+// [N] f32 (may be null), out [M][N] f32.  act: 0 tanh, 1 ELU, -1 identity.  Synchronous;
+// returns 0, or nonzero with the last error set.
+int g1_gemm_bf16_tc(int M, int N, int K, const void* X, int ldx, const void* W, const float* bias, int act, float* out) {
+    if (M <= 0 || N <= 0 || K <= 0 || ldx < K) { set_error(-22, "g1_gemm_bf16_tc", "invalid shape"); return -22; }
+    int* derr = nullptr;
+    CKR(cudaMalloc(&derr, sizeof(int)), -1);
+    CKR(cudaMemset(derr, 0, sizeof(int)), -1);
+    cudaError_t e = dense_tc(M, N, K, (const __nv_bfloat16*)X, ldx, (const __nv_bfloat16*)W, bias, act, out, N, nullptr, 0,
+                             derr, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    int herr = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(derr);
+    if (e != cudaSuccess) { set_error((int)e, "g1_gemm_bf16_tc", cudaGetErrorString(e)); return -1; }
+    if (herr) { set_error(-62, "g1_gemm_bf16_tc", "tensor-core wait timed out"); return -62; }
+    return 0;
+}
 
 // g1_env.cu:365-382
 void g1_occupancy_report(void) {

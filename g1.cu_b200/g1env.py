@@ -49,6 +49,8 @@ SIGNATURES = {
     "g1_env_get_state": (None, [_vp, _vp, _vp, _vp, _vp, _vp]),
     "g1_env_set_state": (None, [_vp, _vp, _vp, _vp, _vp, ctypes.c_ulonglong]),
     "g1_env_ncon_hist": (None, [_vp, ctypes.c_int, _vp]),
+    "g1_gemm_bf16_tc": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int,
+                                       _vp]),
     "g1_qacc_batch": (ctypes.c_int, [ctypes.c_int] + [_vp] * 4 + [ctypes.c_int, ctypes.c_float] + [_vp] * 5),
 }
 
@@ -208,6 +210,21 @@ def qacc_batch(qpos, qvel, tau=None, bdt=None, pgs_iters=8, mu=0.6):
     bdt = None if bdt is None else bdt.expand(n, NV).contiguous().float()
     rc = lib.g1_qacc_batch(n, _dp(qpos), _dp(qvel), _dp(tau), _dp(bdt), pgs_iters, float(mu),
                            *[_dp(out[k]) for k in ("qacc", "qacc_smooth", "bias", "f", "ncon")])
+    if rc:
+        _check()
+    return out
+
+
+def gemm_bf16_tc(X, W, bias=None, act=-1):
+    """out = act(X W^T + b) on the tensor cores (tcgen05).  X [M,K], W [N,K] bf16 CUDA tensors."""
+    _require_gpu()
+    lib = load_library()
+    M, K = X.shape
+    N = W.shape[0]
+    out = torch.empty(M, N, dtype=torch.float32, device=X.device)
+    X = X.contiguous(); W = W.contiguous()
+    b = None if bias is None else bias.float().contiguous()
+    rc = lib.g1_gemm_bf16_tc(M, N, K, _dp(X), K, _dp(W), _dp(b), act, _dp(out))
     if rc:
         _check()
     return out

@@ -111,6 +111,13 @@ void g1_env_ncon_hist(void* h, int enable, unsigned long long* out);
 int g1_qacc_batch(int n, const float* qpos, const float* qvel, const float* tau, const float* bdt, int pgs_iters,
                   float mu, float* qacc, float* qacc_smooth, float* bias, float* f, int* ncon);
 
+/* extension: one dense policy layer out = act(X W^T + b) on the tensor cores (tcgen05, bf16
+ * X [M][K] (row stride ldx) and W [N][K], fp32 bias [N] or NULL, fp32 out [M][N]; act 0 tanh,
+ * 1 ELU, -1 identity).  DEVICE pointers; synchronous; 0 on success.  The building block of
+ * the large-policy rollout (reference counterpart: the per-world mlp_forward layers,
+ * g1_env.cu:229-237, batched over worlds). */
+int g1_gemm_bf16_tc(int M, int N, int K, const void* X, int ldx, const void* W, const float* bias, int act, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -109,6 +109,8 @@ struct Params {
     int* ncon_hist;  // [MAXCON+1] contact-count histogram (substeps), may be null
     int lockstep;    // warps of a CTA walk their worlds in lockstep (named barrier per substep)
     int* ncon_last;  // [N] contact count of each world's last substep (load balancing)
+    int t0;          // trajectory row of the first control step of this launch
+    int ext_policy;  // actions already in A[t0..]: skip the in-kernel policy phase
 };
 
 // ------------------------------------------------------------------ observations
@@ -479,7 +481,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
     int* perm = reinterpret_cast<int*>(frames + NWARPS * plan.group_floats + 4);
     for (int t = 0; t < nsteps; ++t) {
         const uint64_t tick = P.tick0 + (uint64_t)t;
-        if (P.mode == MODE_ROLLOUT) {
+        const int trow = P.t0 + t;
+        if (P.mode == MODE_ROLLOUT && !P.ext_policy) {
             PROF_BEGIN();
             policy_phase(P, T, frames, wbeg, nbw, t, false);
             PROF_MARK(P_POLICY);
@@ -519,7 +522,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
                     for (int s = 0; s < P.S; ++s) substep_barrier();
                 continue;
             }
-            const float* acts = P.mode == MODE_ROLLOUT ? P.A + (size_t)t * P.N * ACT_DIM
+            const float* acts = P.mode == MODE_ROLLOUT ? P.A + (size_t)trow * P.N * ACT_DIM
                               : (P.mode == MODE_STEP ? P.act_in : nullptr);
             float r[GW], d[GW];
             group_control_step(P, T, grp, cw, wid, nvalid, acts, tick, r, d);
@@ -530,8 +533,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
                 if (sl == lane) { my_w = wid[sl]; my_r = r[sl]; my_d = d[sl]; }
             if (lane < nvalid) {
                 if (P.mode == MODE_ROLLOUT) {
-                    P.R[(size_t)t * P.N + my_w] = my_r;
-                    P.D[(size_t)t * P.N + my_w] = my_d;
+                    P.R[(size_t)trow * P.N + my_w] = my_r;
+                    P.D[(size_t)trow * P.N + my_w] = my_d;
                 } else if (P.mode == MODE_STEP) {
                     P.rew_out[my_w] = my_r;
                     P.done_out[my_w] = my_d;
@@ -556,7 +559,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
             PROF_MARK(P_WAIT);
         }
     }
-    if (P.mode == MODE_ROLLOUT) policy_phase(P, T, frames, wbeg, nbw, 0, true);
+    if (P.mode == MODE_ROLLOUT && !P.ext_policy) policy_phase(P, T, frames, wbeg, nbw, 0, true);
 }
 
 // Per-state FK + generalised acceleration (the reference's test_envqacc.cu harness
@@ -611,6 +614,89 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, 
         if (ncon_out && lane < nvalid) ncon_out[s0 + lane] = ncon[lane];
         __syncwarp();
     }
+}
+
+// ------------------------------------------------------------------ large-policy pipeline
+// For policies run on the tensor cores the control step is split into launches: observations
+// (k_obs_norm) -> one tcgen05 dense layer per MLP layer (bf16 activations in HBM/L2) -> head
+// -> sampling (k_sample) -> one physics step of k_g1 with the actions already in A[t].
+#define XK 104  // padded observation width of the bf16 activations (multiple of 8)
+
+// raw obs -> O[row] (row >= 0), normalised + clipped obs -> Xb [N][XK] bf16 (g1_env.cu:297-304)
+__global__ void k_obs_norm(Params P, int row, __nv_bfloat16* Xb) {
+    const int w = blockIdx.x * blockDim.y + threadIdx.y;
+    if (w >= P.N) return;
+    const G1Tables& T = c_tab;
+    const float* qp = P.qp + (size_t)w * NQ;
+    const float* qv = P.qv + (size_t)w * NV;
+    const float* pa = P.pa + (size_t)w * NU;
+    for (int i = threadIdx.x; i < XK; i += blockDim.x) {
+        float z = 0.f;
+        if (i < OBS_DIM) {
+            const float o = obs_elem(i, qp, qv, pa, T);
+            if (row >= 0) P.O[((size_t)row * P.N + w) * OBS_DIM + i] = o;
+            z = (o - P.mean[i]) / sqrtf(P.var[i] + 1e-8f);
+            if (z < -10.f) z = -10.f; else if (z > 10.f) z = 10.f;
+        }
+        Xb[(size_t)w * XK + i] = __float2bfloat16(z);
+    }
+}
+
+// Gaussian actions and log-probabilities from the head outputs HD [N][32] (29 means, value)
+// (g1_env.cu:308-318); row < 0: only the bootstrap value -> Vlast
+__global__ void k_sample(Params P, int row, const float* HD, const float* ls, uint64_t tick) {
+    const int w = blockIdx.x * blockDim.x + threadIdx.x;
+    if (w >= P.N) return;
+    const float* hd = HD + (size_t)w * 32;
+    if (row < 0) { P.Vlast[w] = hd[29]; return; }
+    const float LOG2PI = 1.8378770664093453f;
+    const size_t sb = (size_t)row * P.N + w;
+    float lps = 0.f;
+    for (int i = 0; i < ACT_DIM; ++i) {
+        const uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)w, tick, RNG_ACTION, (uint32_t)i);
+        const float nz = sqrtf(-2.f * logf(u01_open(rb.x))) * cosf(6.283185307179586f * u01(rb.y));
+        const float a = hd[i] + expf(ls[i]) * nz;
+        lps += -0.5f * nz * nz - ls[i] - 0.5f * LOG2PI;
+        P.A[sb * ACT_DIM + i] = a;
+    }
+    P.LP[sb] = lps;
+    P.V[sb] = hd[29];
+}
+
+// torch-ordered fp32 weights (ppo_fused.py:35-44) -> bf16 [out][in] per layer (layer 0's
+// inputs padded to XK with zeros), fp32 biases; head: 29 mean rows, the value row, 2 zero
+// rows; log_std.  seg: per layer {src W offset, src b offset, dst W offset, nin, nout,
+// nin_pad}, the head as layer nh.
+struct RepackPlan {
+    int nl;
+    long long srcW[MAX_HIDDEN + 1], srcB[MAX_HIDDEN + 1], dstW[MAX_HIDDEN + 1], dstB[MAX_HIDDEN + 1];
+    int nin[MAX_HIDDEN + 1], nout[MAX_HIDDEN + 1], ninp[MAX_HIDDEN + 1];
+    long long srcLS;
+};
+__global__ void k_repack_bf16(const float* W, __nv_bfloat16* Wb, float* Bf, float* LS, RepackPlan R) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
+    for (int l = 0; l <= R.nl; ++l) {
+        const bool head = l == R.nl;
+        const int nin = R.nin[l], ninp = R.ninp[l], nout = head ? 32 : R.nout[l];
+        for (size_t e = tid; e < (size_t)nout * ninp; e += nth) {
+            const int o = (int)(e / ninp), i = (int)(e % ninp);
+            float v = 0.f;
+            if (i < nin) {
+                if (!head) v = W[R.srcW[l] + (size_t)o * nin + i];
+                else if (o < ACT_DIM) v = W[R.srcW[l] + (size_t)o * nin + i];
+                else if (o == ACT_DIM) v = W[R.srcW[l] + (size_t)ACT_DIM * nin + ACT_DIM + i];  // Wv after bmu
+            }
+            Wb[R.dstW[l] + e] = __float2bfloat16(v);
+        }
+        for (size_t e = tid; e < (size_t)nout; e += nth) {
+            float b = 0.f;
+            if (!head) b = W[R.srcB[l] + e];
+            else if (e < ACT_DIM) b = W[R.srcB[l] + e];
+            else if (e == ACT_DIM) b = W[R.srcB[l] + ACT_DIM + nin];  // bv
+            Bf[R.dstB[l] + e] = b;
+        }
+    }
+    for (size_t e = tid; e < 32; e += nth) LS[e] = e < ACT_DIM ? W[R.srcLS + e] : 0.f;
 }
 
 // Reset: stand pose + U(+-0.02) joint noise (k_reset, g1_env.cu:97-111); obs optional.
@@ -685,6 +771,11 @@ struct EnvState {
     int sm_count;
     int* ncon_hist;
     int* ncon_last;
+    int prec;                           // 0: fp32 in-kernel policy, 1: bf16 tensor-core policy
+    __nv_bfloat16 *Xb, *Hb[2], *Wb;     // large-policy activations and weights
+    float *Bf, *LS, *HD;
+    int* derr;
+    size_t tc_N, tc_w, tc_wb;
     cudaStream_t stream;                // 0 = legacy default stream (the reference's)
 };
 
@@ -716,7 +807,7 @@ static Params base_params(EnvState* E) {
     P.lockstep = getenv("G1_LOCKSTEP") ? atoi(getenv("G1_LOCKSTEP")) : 1;
     // worlds per CTA: spread over all SMs, at most MAX_WB (then CTAs run in waves)
     int wb = (E->N + E->sm_count - 1) / E->sm_count;
-    if (wb > MAX_WB) wb = MAX_WB;
+    if (wb > 2 * GW * NWARPS) wb = 2 * GW * NWARPS;  // large N: blocks of two full rounds of groups
     if (wb < 1) wb = 1;
     P.wb = wb;
     return P;
@@ -761,6 +852,93 @@ static cudaError_t dense_tc(int M, int N, int K, const __nv_bfloat16* X, int ldx
     if (N <= 32) return launch_dense_tc<32>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
     if (N <= 64) return launch_dense_tc<64>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
     return launch_dense_tc<256>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+}
+
+// The large-policy rollout: per control step obs -> tcgen05 layers -> sampling -> physics.
+static void rollout_tc(EnvState* E, int H, const float* W, const float* mean, const float* var, float* O, float* A,
+                       float* LP, float* V, float* R, float* D, float* Vlast) {
+    const int N = E->N, nh = E->nh;
+    int maxw = 32;
+    for (int l = 0; l < nh; ++l) maxw = E->hid[l] > maxw ? E->hid[l] : maxw;
+    RepackPlan RP;
+    memset(&RP, 0, sizeof RP);
+    RP.nl = nh;
+    long long src = 0, dw = 0, db = 0;
+    int nin = OBS_DIM;
+    for (int l = 0; l <= nh; ++l) {
+        const bool head = l == nh;
+        const int no = head ? 32 : E->hid[l];
+        RP.srcW[l] = src; RP.nin[l] = nin; RP.ninp[l] = l == 0 ? XK : nin; RP.nout[l] = no;
+        RP.srcB[l] = src + (long long)(head ? ACT_DIM : no) * nin;
+        RP.dstW[l] = dw; RP.dstB[l] = db;
+        dw += (long long)no * RP.ninp[l];
+        db += no;
+        if (!head) { src += (long long)nin * no + no; nin = no; }
+    }
+    RP.srcLS = src + (long long)ACT_DIM * nin + ACT_DIM + nin + 1;
+    // buffers (allocated on first use, kept by the env)
+    if (E->tc_N < (size_t)N || E->tc_w < (size_t)maxw) {
+        cudaFree(E->Xb); cudaFree(E->Hb[0]); cudaFree(E->Hb[1]); cudaFree(E->HD);
+        E->Xb = E->Hb[0] = E->Hb[1] = nullptr; E->HD = nullptr;
+        CKR(cudaMalloc(&E->Xb, (size_t)N * XK * 2), );
+        CKR(cudaMalloc(&E->Hb[0], (size_t)N * maxw * 2), );
+        CKR(cudaMalloc(&E->Hb[1], (size_t)N * maxw * 2), );
+        CKR(cudaMalloc(&E->HD, (size_t)N * 32 * 4), );
+        E->tc_N = N; E->tc_w = maxw;
+    }
+    if (E->tc_wb < (size_t)dw) {
+        cudaFree(E->Wb); cudaFree(E->Bf); cudaFree(E->LS);
+        CKR(cudaMalloc(&E->Wb, (size_t)dw * 2), );
+        CKR(cudaMalloc(&E->Bf, (size_t)db * 4), );
+        CKR(cudaMalloc(&E->LS, 32 * 4), );
+        E->tc_wb = dw;
+    }
+    if (!E->derr) { CKR(cudaMalloc(&E->derr, sizeof(int)), ); CKR(cudaMemset(E->derr, 0, sizeof(int)), ); }
+    k_repack_bf16<<<240, 256, 0, E->stream>>>(W, E->Wb, E->Bf, E->LS, RP);
+    CKR(cudaGetLastError(), );
+    Params P = base_params(E);
+    P.mode = MODE_ROLLOUT; P.H = 1; P.ext_policy = 1;
+    P.mean = mean; P.var = var;
+    P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
+    const dim3 oblk(32, 8);
+    const int ogrid = (N + 7) / 8;
+    auto policy = [&](int row, uint64_t tick) -> bool {
+        k_obs_norm<<<ogrid, oblk, 0, E->stream>>>(P, row, E->Xb);
+        if (cudaGetLastError() != cudaSuccess) return false;
+        const __nv_bfloat16* in = E->Xb;
+        int k = XK;
+        for (int l = 0; l < nh; ++l) {
+            __nv_bfloat16* out = E->Hb[l & 1];
+            cudaError_t e = dense_tc(N, E->hid[l], k, in, k, E->Wb + RP.dstW[l], E->Bf + RP.dstB[l], E->act, nullptr, 0,
+                                     out, E->hid[l], E->derr, E->stream);
+            if (e != cudaSuccess) { set_error((int)e, "rollout_tc", cudaGetErrorString(e)); return false; }
+            in = out;
+            k = E->hid[l];
+        }
+        cudaError_t e = dense_tc(N, 32, k, in, k, E->Wb + RP.dstW[nh], E->Bf + RP.dstB[nh], -1, E->HD, 32, nullptr, 0,
+                                 E->derr, E->stream);
+        if (e != cudaSuccess) { set_error((int)e, "rollout_tc", cudaGetErrorString(e)); return false; }
+        k_sample<<<(N + 127) / 128, 128, 0, E->stream>>>(P, row, E->HD, E->LS, tick);
+        return cudaGetLastError() == cudaSuccess;
+    };
+    for (int t = 0; t < H; ++t) {
+        const uint64_t tick = E->tick + (uint64_t)t;
+        if (!policy(t, tick)) { set_error(-1, "rollout_tc", "policy launch failed"); return; }
+        P.t0 = t; P.tick0 = tick;
+        if (!launch_g1(E, P)) return;
+    }
+    P.tick0 = E->tick + (uint64_t)H;
+    if (!policy(-1, 0)) { set_error(-1, "rollout_tc", "policy launch failed"); return; }
+    E->tick += (uint64_t)H;
+}
+
+// Device error flag of the tensor-core path (a timed-out MMA wait); read and cleared.
+static int tc_error(EnvState* E) {
+    if (!E->derr) return 0;
+    int herr = 0;
+    if (cudaMemcpy(&herr, E->derr, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (herr) cudaMemset(E->derr, 0, sizeof(int));
+    return herr;
 }
 
 // ------------------------------------------------------------------ allocation-free rollout
@@ -847,6 +1025,8 @@ void g1_env_destroy(void* h) {  // g1_env.cu:469-474
     cudaFree(E->qp); cudaFree(E->qv); cudaFree(E->pa); cudaFree(E->steps);
     cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone);
     cudaFree(E->WT); cudaFree(E->ncon_hist); cudaFree(E->ncon_last);
+    cudaFree(E->Xb); cudaFree(E->Hb[0]); cudaFree(E->Hb[1]); cudaFree(E->Wb); cudaFree(E->Bf); cudaFree(E->LS);
+    cudaFree(E->HD); cudaFree(E->derr);
     delete E;
 }
 
@@ -863,6 +1043,29 @@ int g1_env_set_policy(void* h, int nh, const int* hidden, int activation) {
     size_t need = (size_t)MAX_WB * XSTR + 2 * (size_t)MAX_WB * (((maxw + 3) & ~3) + 4) + KT * OC;
     if (need > (size_t)NWARPS * GROUP_FLOATS) { set_error(-22, "g1_env_set_policy", "hidden width too large for this build"); return -22; }
     E->nh = nh; E->act = activation;
+    for (int i = 0; i < MAX_HIDDEN; ++i) E->hid[i] = i < nh ? hidden[i] : 0;
+    return 0;
+}
+
+// extension: policy precision 1 runs the MLP on the tensor cores in bf16 (fp32 accumulation)
+// as separate launches per control step; widths multiple of 8, up to 1024.
+int g1_env_set_policy_ex(void* h, int nh, const int* hidden, int activation, int precision) {
+    EnvState* E = (EnvState*)h;
+    if (precision == 0) {
+        int rc = g1_env_set_policy(h, nh, hidden, activation);
+        if (rc == 0) E->prec = 0;
+        return rc;
+    }
+    if (precision != 1 || nh < 1 || nh > MAX_HIDDEN || activation < 0 || activation > 1) {
+        set_error(-22, "g1_env_set_policy_ex", "invalid");
+        return -22;
+    }
+    for (int i = 0; i < nh; ++i)
+        if (hidden[i] < 8 || hidden[i] > 1024 || (hidden[i] & 7)) {
+            set_error(-22, "g1_env_set_policy_ex", "bf16 widths must be multiples of 8 in [8, 1024]");
+            return -22;
+        }
+    E->nh = nh; E->act = activation; E->prec = 1;
     for (int i = 0; i < MAX_HIDDEN; ++i) E->hid[i] = i < nh ? hidden[i] : 0;
     return 0;
 }
@@ -908,6 +1111,10 @@ void g1_rollout(void* h, int H, const float* W, const float* mean, const float* 
                 float* V, float* R, float* D, float* Vlast) {
     EnvState* E = (EnvState*)h;
     if (H <= 0) return;
+    if (E->prec == 1) {
+        rollout_tc(E, H, W, mean, var, O, A, LP, V, R, D, Vlast);
+        return;
+    }
     size_t need = policy_floats(E->nh, E->hid);
     if (need > E->WT_cap) {
         cudaFree(E->WT);
@@ -1074,6 +1281,10 @@ int g1_gemm_bf16_tc(int M, int N, int K, const void* X, int ldx, const void* W, 
     if (herr) { set_error(-62, "g1_gemm_bf16_tc", "tensor-core wait timed out"); return -62; }
     return 0;
 }
+
+// extension: nonzero if a tensor-core wait of this env's bf16 policy path timed out since
+// the last call (synchronises the env's device work; the flag is cleared).
+int g1_env_tc_status(void* h) { return tc_error((EnvState*)h); }
 
 // g1_env.cu:365-382
 void g1_occupancy_report(void) {

@@ -46,6 +46,8 @@ SIGNATURES = {
     "g1_env_set_stream": (None, [_vp, _vp]),
     "g1_env_set_policy": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int]),
     "g1_env_set_friction": (None, [_vp, ctypes.c_float]),
+    "g1_env_set_policy_ex": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int]),
+    "g1_env_tc_status": (ctypes.c_int, [_vp]),
     "g1_env_get_state": (None, [_vp, _vp, _vp, _vp, _vp, _vp]),
     "g1_env_set_state": (None, [_vp, _vp, _vp, _vp, _vp, ctypes.c_ulonglong]),
     "g1_env_ncon_hist": (None, [_vp, ctypes.c_int, _vp]),
@@ -133,11 +135,17 @@ class G1Env:
     def set_stream(self, stream):
         _lib.g1_env_set_stream(self.h, ctypes.c_void_p(stream.cuda_stream if stream is not None else 0))
 
-    def set_policy(self, hidden=(256, 256), activation="tanh"):
+    def set_policy(self, hidden=(256, 256), activation="tanh", precision="fp32"):
+        """precision "fp32": the in-kernel fp32 policy (the reference's arithmetic);
+        "bf16": tensor-core policy for wide MLPs."""
         hid = np.ascontiguousarray(hidden, np.int32)
-        rc = _lib.g1_env_set_policy(self.h, len(hidden), _dp(hid), 0 if activation == "tanh" else 1)
+        rc = _lib.g1_env_set_policy_ex(self.h, len(hidden), _dp(hid), 0 if activation == "tanh" else 1,
+                                       0 if precision == "fp32" else 1)
         if rc:
             _check()
+
+    def tc_status(self):
+        return _lib.g1_env_tc_status(self.h)
 
     def set_friction(self, mu):
         _lib.g1_env_set_friction(self.h, float(mu))

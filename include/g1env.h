@@ -91,6 +91,16 @@ void g1_env_set_stream(void* h, void* stream);
  * <= 1024), activation 0 = tanh (the reference's AC, ppo.py:85-99), 1 = ELU. */
 int g1_env_set_policy(void* h, int nh, const int* hidden, int activation);
 
+/* extension: policy_precision 1 runs the MLP on the tensor cores (tcgen05, bf16 weights and
+ * activations, fp32 accumulation) as separate launches per control step, for wide policies
+ * (widths multiple of 8, up to 1024); 0 = the fp32 in-kernel policy of
+ * g1_env_set_policy.  Returns 0 on success. */
+int g1_env_set_policy_ex(void* h, int nh, const int* hidden, int activation, int policy_precision);
+
+/* extension: nonzero if a tensor-core wait of the bf16 policy path timed out since the last
+ * call (synchronous; clears the flag). */
+int g1_env_tc_status(void* h);
+
 /* extension: foot friction coefficient mu of the pyramidal cone (default 0.6). */
 void g1_env_set_friction(void* h, float mu);
 

@@ -22,6 +22,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -111,6 +112,14 @@ struct Params {
     int* ncon_last;  // [N] contact count of each world's last substep (load balancing)
     int t0;          // trajectory row of the first control step of this launch
     int ext_policy;  // actions already in A[t0..]: skip the in-kernel policy phase
+    // fp32 policy on the tensor cores (split-bf16, g1_mlp_tc.cuh tf_layer): chunk images and
+    // biases from k_repack_tf; 0 = the FFMA path (cta_dense) over WT
+    int tf_mlp;
+    const __nv_bfloat16* tf_img;
+    const float* tf_bias;
+    long long tf_woff[MAX_HIDDEN + 1];
+    int tf_boff[MAX_HIDDEN + 1], tf_lsoff;
+    int* tf_err;
 };
 
 // ------------------------------------------------------------------ observations
@@ -227,13 +236,70 @@ __device__ __noinline__ void cta_dense(const float* __restrict__ WT, int wstr, c
 // The block's actions go to A[t] (the physics phase reads them back from there).
 // k_rollout body, g1_env.cu:296-318.
 // final_value: only the value head is used (bootstrap Vlast, g1_env.cu:325-332).
+__device__ __forceinline__ void policy_sample(const Params& P, const float* HD, const float* lsp, int wbeg, int nbw,
+                                              int t, bool final_value);
+
+// tfs (shared memory, tensor-core path only): the g1tc::TfShared pipeline state (mbarriers,
+// TMEM address, phases), kept outside `work`, which the physics phases reuse.
 __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, float* work, int wbeg, int nbw, int t,
-                             bool final_value) {
+                             bool final_value, float* tfs) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* X = work;  // [nbw][XSTR]
     int maxw = 0;
     for (int l = 0; l < P.nh; ++l) maxw = max(maxw, P.hid[l]);
     const int hstr = ((maxw + 3) & ~3) + 4;
+    // FFMA path: X [nbw][XSTR], H0/H1 [nbw][hstr], weight tile.  Tensor-core path
+    // (g1_mlp_tc.cuh): split-bf16 activations A, weight stages, head outputs; the pipeline
+    // state lives in tfs.
+    uint8_t* tf_A = reinterpret_cast<uint8_t*>(((uintptr_t)work + 127) & ~(uintptr_t)127);
+    uint8_t* tf_stages = tf_A + g1tc::TF_ABYTES;
+    float* tf_hd = reinterpret_cast<float*>(tf_stages + g1tc::TF_NSTAGE * g1tc::TF_STAGE);
+    g1tc::TfShared* TS = reinterpret_cast<g1tc::TfShared*>(tfs);
+    auto tf_L = [&](int l) -> g1tc::TfLayer {
+        return g1tc::TfLayer{P.tf_img + P.tf_woff[l], P.tf_bias + P.tf_boff[l], l == 0 ? OBS_DIM : P.hid[l - 1],
+                             l == P.nh ? 32 : P.hid[l]};
+    };
+    if (P.tf_mlp) {
+        // first layer's weights stream in while the observations are built
+        if (threadIdx.x == g1tc::TF_COPY_WARP * 32) {
+            const g1tc::TfLayer L0 = tf_L(0);
+            if (!g1tc::tf_prefetch(TS, tf_stages, L0, TS->st[1])) atomicExch(P.tf_err, 1);
+        }
+        // observations: raw to O, normalised straight into the three bf16 parts of A (8
+        // inputs per thread; inputs 100..111 zero)
+        for (int e = threadIdx.x; e < nbw * 14; e += NTHREADS) {
+            const int w = e / 14, k0 = (e % 14) * 8, gw = wbeg + w;
+            const float* qp = P.qp + (size_t)gw * NQ;
+            const float* qv = P.qv + (size_t)gw * NV;
+            const float* pa = P.pa + (size_t)gw * NU;
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = k0 + j;
+                float z = 0.f;
+                if (i < OBS_DIM) {
+                    const float o = obs_elem(i, qp, qv, pa, T);
+                    if (!final_value) P.O[((size_t)t * P.N + gw) * OBS_DIM + i] = o;
+                    z = (o - P.mean[i]) / sqrtf(P.var[i] + 1e-8f);
+                    if (z < -10.f) z = -10.f; else if (z > 10.f) z = 10.f;
+                }
+                v[j] = z;
+            }
+            g1tc::tf_store8(tf_A, w, k0, v);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        PROF_BEGIN();
+        for (int l = 0; l <= P.nh; ++l) {
+            const g1tc::TfLayer L = tf_L(l), Ln = l < P.nh ? tf_L(l + 1) : L;
+            g1tc::tf_layer<NTHREADS>(TS, tf_A, tf_stages, L, l < P.nh ? &Ln : nullptr, nbw, l < P.nh ? P.act : -1, tf_hd,
+                                     P.tf_err);
+            PROF_MARK(l == 0 ? P_MLP : (l < P.nh ? P_MLP_L1 : P_MLP_HEAD));
+        }
+        policy_sample(P, tf_hd, P.tf_bias + P.tf_lsoff, wbeg, nbw, t, final_value);
+        PROF_MARK(P_SAMPLE);
+        return;
+    }
+    float* X = work;
     float* H0 = X + MAX_WB * XSTR;
     float* H1 = H0 + MAX_WB * hstr;
     float* WTILE = H1 + MAX_WB * hstr;  // [KT][OC]
@@ -266,14 +332,22 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
         wp += (size_t)nin * no + no;
         in = out; nin = no; istr = hstr;
         __syncthreads();
+        PROF_MARK(l == 0 ? P_MLP : P_MLP_L1);
     }
     // heads: 29 means + value (+2 pad) -> scratch row of 32 in X (X is dead now)
     float* HD = X;
     cta_dense(wp, 32, wp + (size_t)nin * 32, nin, 30, in, istr, HD, 32, nbw, -1, WTILE);
     const float* lsp = wp + (size_t)nin * 32 + 32;
     __syncthreads();
-    PROF_MARK(P_MLP);
-    // sampling: one thread per world, actions in index order (g1_env.cu:308-314)
+    PROF_MARK(P_MLP_HEAD);
+    policy_sample(P, HD, lsp, wbeg, nbw, t, final_value);
+    PROF_MARK(P_SAMPLE);
+}
+
+// sampling: one thread per world, actions in index order (g1_env.cu:308-314); HD [nbw][32]
+// holds the 29 means and the value, lsp the 29 log-stds.
+__device__ __forceinline__ void policy_sample(const Params& P, const float* HD, const float* lsp, int wbeg, int nbw,
+                                              int t, bool final_value) {
     if (threadIdx.x < nbw) {
         const int w = threadIdx.x, gw = wbeg + w;
         const float* hd = HD + w * 32;
@@ -297,7 +371,6 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
         }
     }
     __syncthreads();
-    PROF_MARK(P_SAMPLE);
 }
 
 // ------------------------------------------------------------------ physics phase
@@ -337,11 +410,11 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
     for (int w = 0; w < GW; ++w) bdt_all[w] = T.bdt;
     QaccOpts opt;
     opt.pgs_iters = P.pgs; opt.mu = P.mu; opt.bdt = bdt_all;
-    __syncwarp();
-    for (int s = 0; s < P.S; ++s) {
-        if (P.lockstep) substep_barrier();
-        PROF_BEGIN();
-        // PD torque, clamped to the actuator range; |tau qd| kept per actuator for the energy
+    // PD torque, clamped to the actuator range, and |tau qd| accumulated into the energy
+    // actuator by actuator in index order (g1_env.cu:143-152).  The torque of substep s + 1 is
+    // computed right after substep s integrates (same values; it keeps this small piece of code
+    // next to the integration code, which is still in the instruction cache).
+    auto pd_torque = [&]() {
         for (int it = lane; it < GW * ACT_DIM; it += 32) {
             const int w = it / ACT_DIM, i = it % ACT_DIM;
             float* fr = grp + w * WFLOATS;
@@ -353,12 +426,18 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
             fr[WL::CON + i] = fabsf(pdt * fr[WL::QV + d]);
         }
         __syncwarp();
-        if (lane < GW) {  // energy accumulates actuator by actuator in index order (g1_env.cu:151)
+        if (lane < GW) {
             const float* e = grp + lane * WFLOATS + WL::CON;
             for (int i = 0; i < ACT_DIM; ++i) energy += e[i];
         }
         __syncwarp();
-        PROF_MARK(P_STEP);
+    };
+    __syncwarp();
+    pd_torque();
+    for (int s = 0; s < P.S; ++s) {
+        PROF_BEGIN();
+        if (P.lockstep) substep_barrier();
+        PROF_MARK(P_BAR);
         int ncon[GW];
         group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon);
         if (P.ncon_hist && lane == 0)
@@ -374,6 +453,8 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
             group_integrate(grp, T, lane, true);
             if (lane < GW) vx_sum += grp[lane * WFLOATS + WL::QV];
             PROF_MARK(P_INTEG);
+            if (s + 1 < P.S) pd_torque();
+            PROF_MARK(P_STEP);
         }
     }
     // reward / termination per world (g1_env.cu:164-197), lane w
@@ -444,15 +525,23 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
 
 // ------------------------------------------------------------------ the kernel
 struct SmemPlan {
-    int tab_floats, group_floats, total_bytes;
+    int tab_floats, group_floats, tf_floats, total_bytes;
 };
+// [tables][NWARPS frames][4 + MAX_WB: perm][16: tensor-core MLP barriers, TMEM slot, context]
 __host__ __device__ inline SmemPlan smem_plan() {
     SmemPlan p;
     p.tab_floats = ((int)((sizeof(G1Tables) + 15) / 16)) * 4;
     p.group_floats = GROUP_FLOATS + GW * 36;  // + per-world damping rows (k_qacc)
-    p.total_bytes = (p.tab_floats + NWARPS * p.group_floats + 4 + MAX_WB) * 4;
+    p.tf_floats = p.tab_floats + NWARPS * p.group_floats + 4 + MAX_WB;
+    p.total_bytes = (p.tf_floats + 16 + 2 * 16) * 4;
     return p;
 }
+static_assert(((((int)((sizeof(G1Tables) + 15) / 16)) * 4 + NWARPS * (GROUP_FLOATS + GW * 36) + 4 + MAX_WB) & 1) == 0,
+              "mbarriers need 8-byte alignment");
+// policy scratch of the tensor-core MLP inside the frames (g1_mlp_tc.cuh: activations,
+// weight stages, head outputs), 128 bytes of alignment slack
+static_assert(128 + g1tc::TF_SCRATCH <= NWARPS * (GROUP_FLOATS + GW * 36) * 4, "tensor-core MLP scratch must fit in the frames");
+static_assert(sizeof(g1tc::TfShared) <= (16 + 2 * 16) * 4, "tensor-core MLP state must fit its smem slot");
 static_assert(MAX_WB * XSTR + 2 * MAX_WB * 260 + KT * OC <= NWARPS * GROUP_FLOATS, "MLP activations must fit in the frames");
 
 __device__ __forceinline__ void load_tables(float* smem) {
@@ -476,6 +565,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
     const int wbeg = blockIdx.x * P.wb;
     const int nbw = min(P.wb, P.N - wbeg);
     if (nbw <= 0) return;
+    // tensor-core MLP: barriers + 256 TMEM columns for the life of this (persistent) CTA
+    float* tfs = smem + plan.tf_floats;
+    const bool use_tf = P.tf_mlp && P.mode == MODE_ROLLOUT && !P.ext_policy;
+    if (use_tf) g1tc::tf_init(reinterpret_cast<g1tc::TfShared*>(tfs));
     const int nsteps = P.mode == MODE_ROLLOUT ? P.H : (P.mode == MODE_PHYS ? P.K : 1);
     const int nrounds = (nbw + GW * NWARPS - 1) / (GW * NWARPS);
     int* perm = reinterpret_cast<int*>(frames + NWARPS * plan.group_floats + 4);
@@ -484,7 +577,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
         const int trow = P.t0 + t;
         if (P.mode == MODE_ROLLOUT && !P.ext_policy) {
             PROF_BEGIN();
-            policy_phase(P, T, frames, wbeg, nbw, t, false);
+            policy_phase(P, T, frames, wbeg, nbw, t, false, tfs);
             PROF_MARK(P_POLICY);
         }
         __syncthreads();
@@ -559,9 +652,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
             PROF_MARK(P_WAIT);
         }
     }
-    if (P.mode == MODE_ROLLOUT && !P.ext_policy) policy_phase(P, T, frames, wbeg, nbw, 0, true);
+    if (P.mode == MODE_ROLLOUT && !P.ext_policy) policy_phase(P, T, frames, wbeg, nbw, 0, true, tfs);
+    if (use_tf) g1tc::tf_release(reinterpret_cast<g1tc::TfShared*>(tfs));
 }
-
 // Per-state FK + generalised acceleration (the reference's test_envqacc.cu harness
 // semantics, with caller states): a warp takes GW states at a time.
 __global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, const float* qvel, const float* tau,
@@ -673,6 +766,56 @@ struct RepackPlan {
     int nin[MAX_HIDDEN + 1], nout[MAX_HIDDEN + 1], ninp[MAX_HIDDEN + 1];
     long long srcLS;
 };
+// fp32 policy -> split-bf16 chunk images for the in-kernel tensor-core MLP (g1_mlp_tc.cuh,
+// tf_layer): per layer, ceil(nin/16) chunks of [w1 | w2 | w3] in the canonical K-major
+// layout; fp32 biases; the head as 32 outputs (29 means, value, 2 zero rows); log_std [32].
+__device__ __forceinline__ void tf_put(__nv_bfloat16* dst, int N, int n, int kk, float v) {
+    __nv_bfloat16 p0, p1, p2;
+    g1tc::split3(v, p0, p1, p2);
+    const int bi = g1tc::tf_bidx(N, n, kk), per = N * g1tc::tf_kc(N);
+    dst[bi] = p0;
+    dst[per + bi] = p1;
+    dst[2 * per + bi] = p2;
+}
+__global__ void k_repack_tf(const float* W, __nv_bfloat16* img, float* bias, float* LS, RepackPlan R) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
+    for (int l = 0; l <= R.nl; ++l) {
+        const bool head = l == R.nl;
+        const int nin = R.nin[l], N = head ? 32 : R.nout[l], kc = g1tc::tf_kc(N), nch = g1tc::tf_nchunk(nin, N);
+        const int per = N * kc;
+        for (size_t e = tid; e < (size_t)nch * per; e += nth) {
+            const int c = (int)(e / per), n = (int)(e % per) / kc, kk = (int)(e % kc);
+            const int k = c * kc + kk;
+            float v = 0.f;
+            if (k < nin) {
+                if (!head || n < ACT_DIM) v = W[R.srcW[l] + (size_t)n * nin + k];
+                else if (n == ACT_DIM) v = W[R.srcW[l] + (size_t)ACT_DIM * nin + ACT_DIM + k];  // Wv after bmu
+            }
+            tf_put(img + R.dstW[l] + (size_t)c * g1tc::tf_chunk_elems(N), N, n, kk, v);
+        }
+        for (size_t e = tid; e < (size_t)N; e += nth) {
+            float b = 0.f;
+            if (!head) b = W[R.srcB[l] + e];
+            else if (e < ACT_DIM) b = W[R.srcB[l] + e];
+            else if (e == ACT_DIM) b = W[R.srcB[l] + ACT_DIM + nin];  // bv
+            bias[R.dstB[l] + e] = b;
+        }
+    }
+    for (size_t e = tid; e < 32; e += nth) LS[e] = e < ACT_DIM ? W[R.srcLS + e] : 0.f;
+}
+
+// one layer W [N][K] (torch layout) -> chunk images + bias copy (the standalone test entry)
+__global__ void k_tf_image_layer(const float* W, const float* b, int K, int N, __nv_bfloat16* img, float* bias) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
+    const int kc = g1tc::tf_kc(N), nch = g1tc::tf_nchunk(K, N), per = N * kc;
+    for (size_t e = tid; e < (size_t)nch * per; e += nth) {
+        const int c = (int)(e / per), n = (int)(e % per) / kc, kk = (int)(e % kc);
+        const int k = c * kc + kk;
+        tf_put(img + (size_t)c * g1tc::tf_chunk_elems(N), N, n, kk, k < K ? W[(size_t)n * K + k] : 0.f);
+    }
+    for (size_t e = tid; e < (size_t)N; e += nth) bias[e] = b ? b[e] : 0.f;
+}
+
 __global__ void k_repack_bf16(const float* W, __nv_bfloat16* Wb, float* Bf, float* LS, RepackPlan R) {
     const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
     for (int l = 0; l <= R.nl; ++l) {
@@ -776,6 +919,9 @@ struct EnvState {
     float *Bf, *LS, *HD;
     int* derr;
     size_t tc_N, tc_w, tc_wb;
+    uint8_t* tf_img;                    // fp32 policy on the tensor cores: chunk images + biases
+    size_t tf_cap;
+    int ffma_only;                      // 1: keep the fp32 policy on the FFMA path
     cudaStream_t stream;                // 0 = legacy default stream (the reference's)
 };
 
@@ -1026,7 +1172,7 @@ void g1_env_destroy(void* h) {  // g1_env.cu:469-474
     cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone);
     cudaFree(E->WT); cudaFree(E->ncon_hist); cudaFree(E->ncon_last);
     cudaFree(E->Xb); cudaFree(E->Hb[0]); cudaFree(E->Hb[1]); cudaFree(E->Wb); cudaFree(E->Bf); cudaFree(E->LS);
-    cudaFree(E->HD); cudaFree(E->derr);
+    cudaFree(E->HD); cudaFree(E->derr); cudaFree(E->tf_img);
     delete E;
 }
 
@@ -1051,9 +1197,9 @@ int g1_env_set_policy(void* h, int nh, const int* hidden, int activation) {
 // as separate launches per control step; widths multiple of 8, up to 1024.
 int g1_env_set_policy_ex(void* h, int nh, const int* hidden, int activation, int precision) {
     EnvState* E = (EnvState*)h;
-    if (precision == 0) {
+    if (precision == 0 || precision == 2) {  // fp32: tensor cores (3xTF32) where eligible / FFMA only
         int rc = g1_env_set_policy(h, nh, hidden, activation);
-        if (rc == 0) E->prec = 0;
+        if (rc == 0) { E->prec = 0; E->ffma_only = precision == 2; }
         return rc;
     }
     if (precision != 1 || nh < 1 || nh > MAX_HIDDEN || activation < 0 || activation > 1) {
@@ -1107,6 +1253,60 @@ void g1_env_step_device(void* h, const float* act, float* obs, float* rew, float
 }
 
 // g1_env.cu:446-453: the fused rollout into caller-owned DEVICE buffers, asynchronous.
+// The fp32 policy runs on the tensor cores (3xTF32) when every hidden width is a multiple of
+// 16 in [16, 256]; other widths, or ffma_only, keep the FFMA path.
+static bool tf_eligible(const EnvState* E) {
+    if (E->ffma_only || E->nh < 1) return false;
+    for (int l = 0; l < E->nh; ++l)
+        if (E->hid[l] < 16 || E->hid[l] > 256 || (E->hid[l] & 15)) return false;
+    return true;
+}
+
+// Builds the chunk images of W (k_repack_tf, on the env stream) and fills the tensor-core
+// fields of P.  Returns false (error set) on allocation failure.
+static bool prepare_tf(EnvState* E, const float* W, Params& P) {
+    RepackPlan RP;
+    memset(&RP, 0, sizeof RP);
+    RP.nl = E->nh;
+    long long src = 0, dw = 0;
+    int db = 0, nin = OBS_DIM;
+    for (int l = 0; l <= E->nh; ++l) {
+        const bool head = l == E->nh;
+        const int no = head ? 32 : E->hid[l];
+        RP.srcW[l] = src; RP.nin[l] = nin; RP.nout[l] = no;
+        RP.srcB[l] = src + (long long)(head ? ACT_DIM : no) * nin;
+        RP.dstW[l] = dw; RP.dstB[l] = db;
+        P.tf_woff[l] = dw; P.tf_boff[l] = db;
+        dw += (long long)g1tc::tf_nchunk(nin, no) * g1tc::tf_chunk_elems(no);
+        db += no;
+        if (!head) { src += (long long)nin * no + no; nin = no; }
+    }
+    RP.srcLS = src + (long long)ACT_DIM * nin + ACT_DIM + nin + 1;
+    const size_t img_bytes = ((size_t)dw * 2 + 255) & ~(size_t)255;
+    const size_t need = img_bytes + ((size_t)db + 32) * 4;
+    if (need > E->tf_cap) {
+        cudaFree(E->tf_img);
+        E->tf_img = nullptr;
+        E->tf_cap = 0;
+        CKR(cudaMalloc(&E->tf_img, need), false);
+        E->tf_cap = need;
+    }
+    if (!E->derr) {
+        CKR(cudaMalloc(&E->derr, sizeof(int)), false);
+        CKR(cudaMemset(E->derr, 0, sizeof(int)), false);
+    }
+    __nv_bfloat16* img = reinterpret_cast<__nv_bfloat16*>(E->tf_img);
+    float* bias = reinterpret_cast<float*>(E->tf_img + img_bytes);
+    k_repack_tf<<<148, 256, 0, E->stream>>>(W, img, bias, bias + db, RP);
+    CKR(cudaGetLastError(), false);
+    P.tf_mlp = 1;
+    P.tf_img = img;
+    P.tf_bias = bias;
+    P.tf_lsoff = db;
+    P.tf_err = E->derr;
+    return true;
+}
+
 void g1_rollout(void* h, int H, const float* W, const float* mean, const float* var, float* O, float* A, float* LP,
                 float* V, float* R, float* D, float* Vlast) {
     EnvState* E = (EnvState*)h;
@@ -1122,9 +1322,13 @@ void g1_rollout(void* h, int H, const float* W, const float* mean, const float* 
         CKR(cudaMalloc(&E->WT, need * 4), );
         E->WT_cap = need;
     }
-    k_repack<<<120, 256, 0, E->stream>>>(W, E->WT, E->nh, E->hid[0], E->hid[1], E->hid[2], E->hid[3]);
-    CKR(cudaGetLastError(), );
     Params P = base_params(E);
+    if (tf_eligible(E)) {
+        if (!prepare_tf(E, W, P)) return;
+    } else {
+        k_repack<<<120, 256, 0, E->stream>>>(W, E->WT, E->nh, E->hid[0], E->hid[1], E->hid[2], E->hid[3]);
+        CKR(cudaGetLastError(), );
+    }
     P.mode = MODE_ROLLOUT; P.H = H;
     P.WT = E->WT; P.mean = mean; P.var = var;
     P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
@@ -1255,8 +1459,8 @@ int g1_qacc_batch(int n, const float* qpos, const float* qvel, const float* tau,
 // since the last call.
 int g1_prof_read(unsigned long long* out) {
     CKR(cudaDeviceSynchronize(), -1);
-    CKR(cudaMemcpyFromSymbol(out, g_prof, sizeof(unsigned long long) * 16), -1);
-    unsigned long long z[16] = {0};
+    CKR(cudaMemcpyFromSymbol(out, g_prof, sizeof(unsigned long long) * 32), -1);
+    unsigned long long z[32] = {0};
     CKR(cudaMemcpyToSymbol(g_prof, z, sizeof z), -1);
     return 0;
 }
@@ -1266,6 +1470,42 @@ int g1_prof_read(unsigned long long* out) {
 // fp32 accumulation).  DEVICE pointers: X [M][K] bf16 (row stride ldx), W [N][K] bf16, bias
 // [N] f32 (may be null), out [M][N] f32.  act: 0 tanh, 1 ELU, -1 identity.  Synchronous;
 // returns 0, or nonzero with the last error set.
+// extension (test entry of the in-kernel fp32 policy layer): out = act(X W^T + b) for
+// rows <= 64, N % 16 == 0, N <= 256, K <= 256, with the split-bf16 tensor-core layer the
+// fused rollout uses (one CTA).  DEVICE pointers X [rows][K], W [N][K], b [N] (may be null),
+// out [rows][N]; act 0 tanh, 1 ELU, -1 identity; synchronous; 0 on success.
+int g1_dense_bf16x3(int rows, int K, int N, const float* X, const float* W, const float* b, int act, float* out) {
+    if (rows < 1 || rows > g1tc::TF_ROWS || K < 1 || K > g1tc::TF_KMAX || N < 16 || N > 256 || (N & 15) || act < -1 ||
+        act > 1) {
+        set_error(-22, "g1_dense_bf16x3", "invalid shape");
+        return -22;
+    }
+    const int nch = g1tc::tf_nchunk(K, N);
+    __nv_bfloat16* img = nullptr;
+    float* bias = nullptr;
+    int* derr = nullptr;
+    CKR(cudaMalloc(&img, (size_t)nch * g1tc::tf_chunk_elems(N) * 2), -1);
+    CKR(cudaMalloc(&bias, (size_t)N * 4), -1);
+    CKR(cudaMalloc(&derr, sizeof(int)), -1);
+    CKR(cudaMemset(derr, 0, sizeof(int)), -1);
+    k_tf_image_layer<<<64, 256>>>(W, b, K, N, img, bias);
+    const int smem = g1tc::tf_test_smem();
+    // identity on a wide layer goes through the hidden-layer epilogue (act 2)
+    const int kact = (act < 0 && N > 32) ? 2 : act;
+    cudaError_t e = cudaFuncSetAttribute(g1tc::k_tf_layer_test<224>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) {
+        g1tc::k_tf_layer_test<224><<<1, 224, smem>>>(rows, K, N, X, img, bias, kact, out, derr);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    int herr = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(img); cudaFree(bias); cudaFree(derr);
+    if (e != cudaSuccess) { set_error((int)e, "g1_dense_bf16x3", cudaGetErrorString(e)); return -1; }
+    if (herr) { set_error(-62, "g1_dense_bf16x3", "tensor-core wait timed out"); return -62; }
+    return 0;
+}
+
 int g1_gemm_bf16_tc(int M, int N, int K, const void* X, int ldx, const void* W, const float* bias, int act, float* out) {
     if (M <= 0 || N <= 0 || K <= 0 || ldx < K) { set_error(-22, "g1_gemm_bf16_tc", "invalid shape"); return -22; }
     int* derr = nullptr;
@@ -1305,3 +1545,6 @@ void g1_occupancy_report(void) {
 }
 
 }  // extern "C"
+
+// trainer batch preparation (GAE, observation renormalisation, RunNorm update)
+#include "g1_ppo_prep.cuh"

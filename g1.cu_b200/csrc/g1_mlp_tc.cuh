@@ -23,7 +23,7 @@ namespace g1tc {
 constexpr int TM = 128;   // rows (worlds) per CTA tile
 constexpr int KC = 64;    // K per chunk
 constexpr int NTH = 128;  // threads per CTA
-constexpr uint32_t SPIN_LIMIT = 1u << 26;
+constexpr uint32_t SPIN_LIMIT = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -215,5 +215,325 @@ template <int BN>
 constexpr int dense_tc_smem() {
     return 2 * (TM * KC * 2 + BN * KC * 2) + 64;
 }
+
+// ======================================================================================
+// fp32-accurate dense layers inside a CTA on the tensor cores (the fp32 policy MLP of the
+// fused rollout kernel).
+//
+// out[r][n] = act(b[n] + sum_k x[r][k] W[n][k]) for r < nrows <= 64, N <= 256 (N % 16 == 0),
+// K <= 256.  Each fp32 operand is split into three bf16 parts, v = v1 + v2 + v3 with
+// v1 = bf16(v), v2 = bf16(v - v1), v3 = bf16(v - v1 - v2) (the differences are exact in fp32;
+// the split keeps 24+ significant bits), and the six products whose size is at least
+// 2^-18 of x*w -- x3w1, x1w3, x2w2, x2w1, x1w2, x1w1, smallest first -- are accumulated in
+// fp32 in tensor memory by `tcgen05.mma.kind::f16` (M = 128, N, K = 16).  The dropped terms
+// are below 2^-26 |x w|, under fp32 rounding (the multi-word split is the classical way to
+// carry a wider mantissa through a narrower multiplier).  The tensor core aligns each MMA's
+// addends to the accumulator it adds into, so small terms added into the running full sum
+// would lose their low bits (measured: ~6x the error of an fp32 dot product at K = 256).  The
+// five small products therefore accumulate in their own TMEM accumulator (columns 256..511)
+// and x1w1 in another (columns 0..N-1); the epilogue adds the two in fp32 -- the result is as
+// accurate as an fp32 FFMA dot product.
+//
+// Activations stay resident in shared memory as the three bf16 parts of the whole input
+// row (A, canonical K-major no-swizzle layout, 64 rows stored); the previous layer's
+// epilogue writes them directly.  Weights come from global memory pre-split: one contiguous
+// image per 16-wide K chunk ([w1 | w2 | w3], canonical), fetched by a single `cp.async.bulk`
+// (no multicast) into one of TF_NSTAGE stages, completing on the stage's `full` mbarrier.
+// One thread walks the chunks (wait full, six MMAs, commit to the stage's `empty` barrier,
+// refill the stage behind), so there is no CTA-wide synchronisation per chunk; a final
+// commit to `done` releases the epilogue.  Every mbarrier wait is bounded; a timeout sets
+// *err (the results are then garbage, nothing faults).
+//
+// Byte layouts:
+//   A part p: p * TF_APART + (k>>3)*1024 + (r>>3)*128 + (r&7)*16 + (k&7)*2.  The M = 128 MMA
+//       also reads rows 64..127 through the row stride; those land in the next 1 KB
+//       (garbage rows, never read back).
+//   B chunk part p (N-wide layer): p * 32N + (k>>3)*16N + (n>>3)*128 + (n&7)*16 + (k&7)*2.
+// Descriptors: LBO = distance between core matrices along K, SBO = 128 (next 8 rows).
+#ifdef G1_PROF  // phase counters of the profiling build (g1_physics.cuh)
+using ::g1::g_prof;
+using ::g1::P_TF_MMA;
+using ::g1::P_TF_EPI;
+#endif
+constexpr int TF_ROWS = 64;
+constexpr int TF_KMAX = 256;
+constexpr int TF_APART = TF_ROWS * TF_KMAX * 2;  // 32 KB per bf16 part
+constexpr int TF_ABYTES = 3 * TF_APART;
+constexpr int TF_STAGE = 3 * 4096 * 2;           // 24 KB: one chunk of N x kc weights, N kc = 4096
+constexpr int TF_NSTAGE = 4;
+constexpr int TF_HDBYTES = TF_ROWS * 32 * 4;     // head outputs, fp32 [64][32]
+constexpr int TF_SCRATCH = TF_ABYTES + TF_NSTAGE * TF_STAGE + TF_HDBYTES;
+constexpr int TF_MMA_WARP = 2, TF_COPY_WARP = 3;  // lane 0 of each; idle in the epilogue (rows < 64)
+
+// K width of one weight chunk of an N-wide layer: the largest multiple of 16 with N kc <= 4096
+__host__ __device__ constexpr int tf_kc(int N) { return ((4096 / N) & ~15) < TF_KMAX ? ((4096 / N) & ~15) : TF_KMAX; }
+
+__device__ __forceinline__ uint64_t make_desc_lbo(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+// global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned),
+// completing on mbarrier `bar`; plain (non-multicast) form
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// split of an fp32 value into three bf16 words (v = p0 + p1 + p2 to 2^-27)
+__device__ __forceinline__ void split3(float v, __nv_bfloat16& p0, __nv_bfloat16& p1, __nv_bfloat16& p2) {
+    p0 = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(p0);
+    p1 = __float2bfloat16_rn(r1);
+    p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+}
+__device__ __forceinline__ uint32_t pack2(__nv_bfloat16 a, __nv_bfloat16 b) {
+    return (uint32_t)__bfloat16_as_ushort(a) | ((uint32_t)__bfloat16_as_ushort(b) << 16);
+}
+// byte offset of (row r, input k) inside one A part
+__host__ __device__ inline uint32_t tf_aoff(int r, int k) {
+    return (uint32_t)((k >> 3) * 1024 + (r >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
+}
+// element index of (n, kk) inside one part of a chunk image of an N-wide layer
+__host__ __device__ inline int tf_bidx(int N, int n, int kk) {
+    return (kk >> 3) * (8 * N) + (n >> 3) * 64 + (n & 7) * 8 + (kk & 7);
+}
+// bf16 elements of one chunk image of an N-wide layer ([w1 | w2 | w3])
+__host__ __device__ constexpr int tf_chunk_elems(int N) { return 3 * N * tf_kc(N); }
+__host__ __device__ constexpr int tf_nchunk(int K, int N) { return (K + tf_kc(N) - 1) / tf_kc(N); }
+
+// writes the 3 parts of 8 consecutive inputs k0..k0+7 (k0 % 8 == 0) of row r
+__device__ __forceinline__ void tf_store8(uint8_t* A, int r, int k0, const float* v) {
+    __nv_bfloat16 p[3][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) split3(v[j], p[0][j], p[1][j], p[2][j]);
+    const uint32_t off = tf_aoff(r, k0);
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+        *reinterpret_cast<uint4*>(A + q * TF_APART + off) =
+            make_uint4(pack2(p[q][0], p[q][1]), pack2(p[q][2], p[q][3]), pack2(p[q][4], p[q][5]), pack2(p[q][6], p[q][7]));
+}
+
+// Shared-memory pipeline state (outlives the caller's other uses of the scratch).  Weight
+// chunks are numbered globally (st[1] = chunks consumed so far); chunk g uses stage g % NSTAGE
+// and is that stage's (g / NSTAGE)-th use, so its full / empty phase parity is (g/NSTAGE) & 1.
+// st = {tmem, chunks consumed, -, -, done phase, chunks of the next layer already issued}.
+struct TfShared {
+    uint64_t bars[2 * TF_NSTAGE + 1];  // full[4], empty[4], done
+    uint32_t st[6];
+};
+// TMEM: 512 columns -- [0, 256) the x1w1 accumulator, [256, 512) the small-product one
+
+struct TfLayer {
+    const __nv_bfloat16* img;  // chunk images
+    const float* bias;         // [N]
+    int K, N;
+};
+
+__device__ __forceinline__ void tf_init(TfShared* S) {
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2 * TF_NSTAGE + 1; ++i) mbar_init(&S->bars[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 1; i < 6; ++i) S->st[i] = 0;
+    }
+    if ((threadIdx.x >> 5) == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S->st[0])),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+}
+
+__device__ __forceinline__ void tf_release(TfShared* S) {
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    if ((threadIdx.x >> 5) == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(S->st[0]), "r"(512));
+}
+
+// copy thread: bring chunk c of layer L in as global chunk g, once the stage's previous
+// chunk (g - NSTAGE) has been consumed by its MMAs
+__device__ __forceinline__ bool tf_issue(TfShared* S, uint8_t* stages, const TfLayer& L, int c, uint32_t g) {
+    const uint32_t s = g % TF_NSTAGE;
+    bool ok = true;
+    if (g >= TF_NSTAGE) ok = mbar_wait(smem_u32(&S->bars[TF_NSTAGE + s]), ((g / TF_NSTAGE) - 1) & 1u);
+    const uint32_t bytes = (uint32_t)tf_chunk_elems(L.N) * 2;
+    mbar_expect_tx(&S->bars[s], bytes);
+    bulk_g2s(stages + s * TF_STAGE, L.img + (size_t)c * tf_chunk_elems(L.N), bytes, &S->bars[s]);
+    return ok;
+}
+
+// copy thread: queue the first chunks of layer L, which starts at global chunk g0
+__device__ __forceinline__ bool tf_prefetch(TfShared* S, uint8_t* stages, const TfLayer& L, uint32_t g0) {
+    const int n = tf_nchunk(L.K, L.N), m = n < TF_NSTAGE ? n : TF_NSTAGE;
+    bool ok = true;
+    for (int c = 0; c < m; ++c) ok &= tf_issue(S, stages, L, c, g0 + c);
+    S->st[5] = (uint32_t)m;
+    return ok;
+}
+
+// One layer.  All threads call it; on entry the A parts of the input are in place (visible
+// to the async proxy: the writers ran fence.proxy.async before the CTA barrier that
+// preceded this call) and tf_prefetch queued the first chunks of L.  The MMA thread walks
+// the chunks (wait full, six MMAs, commit to the stage's empty barrier); the copy thread
+// refills stages as they empty and then queues the first chunks of nxt (if any).  Epilogue:
+// hidden layers (act 0 tanh / 1 ELU / 2 identity) write the 3 parts of their output into A,
+// in place; the head (act -1, N <= 32) writes fp32 to hd [rows][32].
+template <int NT>
+__device__ void tf_layer(TfShared* S, uint8_t* A, uint8_t* stages, const TfLayer& L, const TfLayer* nxt, int nrows, int act,
+                         float* hd, int* err) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int N = L.N, kc = tf_kc(N), nchunk = tf_nchunk(L.K, N);
+    const uint32_t tmem = S->st[0], g0 = S->st[1];
+    bool ok = true;
+#ifdef G1_PROF
+    PROF_BEGIN();
+#endif
+    if (warp == TF_MMA_WARP && lane == 0) {
+        const uint32_t idesc = make_idesc(128, N);
+        const uint32_t pbytes = (uint32_t)N * kc * 2;
+        const uint32_t a0 = smem_u32(A);
+        // operand pairs (A part, B part), smallest product first
+        const int pa[6] = {2, 0, 1, 1, 0, 0}, pb[6] = {0, 2, 1, 0, 1, 0};
+        for (int c = 0; c < nchunk; ++c) {
+            const uint32_t g = g0 + c, s = g % TF_NSTAGE;
+            if (!mbar_wait(smem_u32(&S->bars[s]), (g / TF_NSTAGE) & 1u)) ok = false;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t b0 = smem_u32(stages + s * TF_STAGE);
+            for (int j = 0; j < kc / 16; ++j) {
+                const int kg = c * (kc / 16) + j;  // 16-wide K step within the layer
+                if (kg * 16 >= L.K) break;  // all-zero weights past K (A is zero-padded to 16)
+#pragma unroll
+                for (int m = 0; m < 6; ++m) {
+                    const uint64_t ad = make_desc_lbo(a0 + pa[m] * TF_APART + kg * 2048, 1024, 128);
+                    const uint64_t bd = make_desc_lbo(b0 + pb[m] * pbytes + j * 2 * (16 * N), 16 * N, 128);
+                    // m < 5: small products -> columns 256..; m == 5: x1 w1 -> columns 0..
+                    const uint32_t dst = tmem + (m < 5 ? 256u : 0u);
+                    const uint32_t accum = (kg > 0 || (m > 0 && m < 5)) ? 1u : 0u;
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\t"
+                        "setp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dst),
+                        "l"(ad), "l"(bd), "r"(idesc), "r"(accum));
+                }
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(&S->bars[TF_NSTAGE + s]))
+                         : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&S->bars[2 * TF_NSTAGE]))
+                     : "memory");
+    } else if (warp == TF_COPY_WARP && lane == 0) {
+        for (int c = (int)S->st[5]; c < nchunk; ++c) ok &= tf_issue(S, stages, L, c, g0 + c);
+        if (nxt) ok &= tf_prefetch(S, stages, *nxt, g0 + nchunk);
+        else S->st[5] = 0;
+    }
+    // every thread: wait for the layer's MMAs
+    if (!mbar_wait(smem_u32(&S->bars[2 * TF_NSTAGE]), S->st[4] & 1u)) ok = false;
+    if (!ok) atomicExch(err, 1);
+    asm volatile("tcgen05.fence::after_thread_sync;");
+#ifdef G1_PROF
+    PROF_MARK(P_TF_MMA);
+#endif
+    // epilogue: TMEM lane r = row r; warps w and w+4 share lanes 32(w&3).. and split the columns
+    const int q = warp & 3;
+    const int nshare = (q + 4 < NT / 32) ? 2 : 1;
+    if (32 * q < nrows) {
+        const int half = N / nshare, c_beg = (warp >> 2) * half, row = 32 * q + lane;
+        for (int c0 = c_beg; c0 < c_beg + half; c0 += 8) {
+            uint32_t r[8], u[8];
+            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                : "r"(taddr));
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7])
+                : "r"(taddr + 256u));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float x = (__uint_as_float(r[j]) + __uint_as_float(u[j])) + L.bias[c0 + j];
+                if (act == 0) x = tanhf(x);
+                else if (act == 1) x = x > 0.f ? x : expm1f(x);
+                v[j] = x;
+            }
+            if (row < nrows) {
+                if (act < 0) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) hd[row * 32 + c0 + j] = v[j];
+                } else {
+                    tf_store8(A, row, c0, v);
+                }
+            }
+        }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+#ifdef G1_PROF
+    PROF_MARK(P_TF_EPI);
+#endif
+    if (tid == 0) { S->st[1] = g0 + nchunk; S->st[4] ^= 1u; }
+    __syncthreads();
+}
+
+// Standalone test of tf_layer: one CTA of NT threads, rows <= 64; X [rows][K] fp32 global,
+// W image / bias as built for one layer, out [rows][N] fp32 global.  Runs the layer twice
+// (the second pass exercises the later barrier phases); hidden activations are read back
+// from the A parts (sum of the three words), identity from the head buffer (N <= 32).
+template <int NT>
+__global__ void __launch_bounds__(NT, 1)
+k_tf_layer_test(int rows, int K, int N, const float* X, const __nv_bfloat16* img, const float* bias, int act, float* out,
+                int* err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* A = smem;
+    uint8_t* stages = smem + TF_ABYTES;
+    float* hd = reinterpret_cast<float*>(stages + TF_NSTAGE * TF_STAGE);
+    TfShared* S = reinterpret_cast<TfShared*>(smem + TF_SCRATCH);
+    tf_init(S);
+    TfLayer L{img, bias, K, N};
+    for (int rep = 0; rep < 2; ++rep) {
+        const int kpad = tf_nchunk(K, N) * tf_kc(N) < TF_KMAX ? tf_nchunk(K, N) * tf_kc(N) : TF_KMAX;
+        for (int e = threadIdx.x; e < rows * (kpad / 8); e += NT) {
+            const int r = e / (kpad / 8), k0 = (e % (kpad / 8)) * 8;
+            float v[8];
+            for (int j = 0; j < 8; ++j) v[j] = k0 + j < K ? X[r * K + k0 + j] : 0.f;
+            tf_store8(A, r, k0, v);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (threadIdx.x == TF_COPY_WARP * 32) tf_prefetch(S, stages, L, S->st[1]);
+        tf_layer<NT>(S, A, stages, L, nullptr, rows, act, hd, err);
+    }
+    for (int e = threadIdx.x; e < rows * N; e += NT) {
+        const int r = e / N, n = e % N;
+        float v;
+        if (act < 0) v = hd[r * 32 + n];
+        else {
+            const uint32_t off = tf_aoff(r, n);
+            v = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(A + off)) +
+                __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(A + TF_APART + off)) +
+                __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(A + 2 * TF_APART + off));
+        }
+        out[e] = v;
+    }
+    tf_release(S);
+}
+__host__ __device__ constexpr int tf_test_smem() { return TF_SCRATCH + (int)sizeof(TfShared); }
 
 }  // namespace g1tc

@@ -53,6 +53,11 @@ SIGNATURES = {
     "g1_env_ncon_hist": (None, [_vp, ctypes.c_int, _vp]),
     "g1_gemm_bf16_tc": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int,
                                        _vp]),
+    "g1_dense_bf16x3": (ctypes.c_int, [ctypes.c_int] * 3 + [_vp] * 3 + [ctypes.c_int, _vp]),
+    "g1_gae": (ctypes.c_int, [ctypes.c_int, ctypes.c_int] + [_vp] * 4 + [ctypes.c_double, ctypes.c_double] + [_vp] * 4),
+    "g1_obs_prep": (ctypes.c_int, [ctypes.c_longlong, ctypes.c_int] + [_vp] * 6),
+    "g1_adv_normalize": (ctypes.c_int, [ctypes.c_longlong, _vp, _vp, _vp]),
+    "g1_runnorm_update": (ctypes.c_int, [ctypes.c_int, _vp, _vp, ctypes.c_double, _vp, _vp]),
     "g1_qacc_batch": (ctypes.c_int, [ctypes.c_int] + [_vp] * 4 + [ctypes.c_int, ctypes.c_float] + [_vp] * 5),
 }
 
@@ -136,11 +141,12 @@ class G1Env:
         _lib.g1_env_set_stream(self.h, ctypes.c_void_p(stream.cuda_stream if stream is not None else 0))
 
     def set_policy(self, hidden=(256, 256), activation="tanh", precision="fp32"):
-        """precision "fp32": the in-kernel fp32 policy (the reference's arithmetic);
+        """precision "fp32": the in-kernel fp32-accurate policy (split-bf16 on the tensor cores when
+        every hidden width is a multiple of 16 up to 256, else FFMA); "fp32-ffma": always FFMA;
         "bf16": tensor-core policy for wide MLPs."""
         hid = np.ascontiguousarray(hidden, np.int32)
-        rc = _lib.g1_env_set_policy_ex(self.h, len(hidden), _dp(hid), 0 if activation == "tanh" else 1,
-                                       0 if precision == "fp32" else 1)
+        code = {"fp32": 0, "bf16": 1, "fp32-ffma": 2}[precision]
+        rc = _lib.g1_env_set_policy_ex(self.h, len(hidden), _dp(hid), 0 if activation == "tanh" else 1, code)
         if rc:
             _check()
 
@@ -236,6 +242,75 @@ def gemm_bf16_tc(X, W, bias=None, act=-1):
     if rc:
         _check()
     return out
+
+
+def dense_bf16x3(X, W, bias=None, act=-1):
+    """out = act(X W^T + b) with the rollout kernel's split-bf16 tensor-core layer (rows <= 64)."""
+    _require_gpu()
+    lib = load_library()
+    X = X.float().contiguous(); W = W.float().contiguous()
+    rows, K = X.shape
+    N = W.shape[0]
+    out = torch.empty(rows, N, dtype=torch.float32, device=X.device)
+    b = None if bias is None else bias.float().contiguous()
+    if lib.g1_dense_bf16x3(rows, K, N, _dp(X), _dp(W), _dp(b), act, _dp(out)):
+        _check()
+    return out
+
+
+# ---------------- trainer batch preparation (ppo_fused.py:104-119, ppo.py:71-79) ----------------
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def gae_device(R, V, D, Vlast, gamma=0.99, lam=0.95):
+    """adv, ret [H,N] and the fp64 advantage moments [count, sum, sumsq] (g1_gae), on torch's
+    current stream.  adv/ret are bit-identical to the reference's torch GAE loop."""
+    _require_gpu()
+    lib = load_library()
+    H, N = R.shape
+    adv, ret = torch.empty_like(R), torch.empty_like(R)
+    mom = torch.empty(3, dtype=torch.float64, device=R.device)
+    Rc, Vc, Dc, Lc = (t.contiguous() for t in (R, V, D, Vlast))
+    if lib.g1_gae(H, N, _dp(Rc), _dp(Vc), _dp(Dc), _dp(Lc), gamma, lam, _dp(adv), _dp(ret), _dp(mom), _stream()):
+        _check()
+    return adv, ret, mom
+
+
+def obs_prep_device(O, fmean, fvar):
+    """nobs = clamp((O - fmean)/sqrt(fvar + 1e-8), -10, 10) and the fp64 raw-observation
+    moments [rows, sum[dim], sumsq[dim]] in one pass (g1_obs_prep)."""
+    _require_gpu()
+    lib = load_library()
+    dim = O.shape[-1]
+    Oc = O.contiguous()
+    rows = Oc.numel() // dim
+    nobs = torch.empty_like(Oc)
+    mom = torch.empty(1 + 2 * dim, dtype=torch.float64, device=O.device)
+    fm, fv = fmean.float().contiguous(), fvar.float().contiguous()
+    if lib.g1_obs_prep(rows, dim, _dp(Oc), _dp(fm), _dp(fv), _dp(nobs), _dp(mom), _stream()):
+        _check()
+    return nobs, mom
+
+
+def adv_normalize_device(adv, adv_mom):
+    """In place: adv = (adv - mean)/(std + 1e-8) from (possibly all-reduced) moments."""
+    lib = load_library()
+    assert adv.is_contiguous()
+    if lib.g1_adv_normalize(adv.numel(), _dp(adv), _dp(adv_mom), _stream()):
+        _check()
+    return adv
+
+
+def runnorm_update_device(norm, obs_mom, rows_total):
+    """RunNorm.update (ppo.py:71-79) on the device from (possibly all-reduced) moments;
+    rows_total = obs_mom[0], known on the host so nothing synchronises."""
+    lib = load_library()
+    assert norm.mean.is_contiguous() and norm.var.is_contiguous()
+    if lib.g1_runnorm_update(norm.mean.numel(), _dp(norm.mean), _dp(norm.var), float(norm.count), _dp(obs_mom),
+                             _stream()):
+        _check()
+    norm.count = norm.count + rows_total
 
 
 # ---------------- running obs normalizer (ppo.py:63-81) ----------------

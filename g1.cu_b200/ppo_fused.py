@@ -6,10 +6,11 @@ training loop, ppo_fused.py:47-171, with world sharding across ranks).
 
 The rollout runs in the CUDA library (g1_rollout); torch does only the PPO update, reading
 the trajectory buffers in place.  With WORLD_SIZE > 1 each rank owns its own worlds (global
-world ids rank*N + i, so RNG streams are disjoint) and three things cross NCCL:
-  * the RunNorm moments of the raw observations (so every rank keeps the same frozen
-    normaliser, ppo_fused.py:104-106),
-  * the advantage moments for advantage normalisation (ppo_fused.py:119),
+world ids rank*N + i, so RNG streams are disjoint) and two things cross NCCL:
+  * one fp64 buffer of batch moments -- the raw-observation sums for the RunNorm update (so
+    every rank keeps the same frozen normaliser, ppo_fused.py:104-106) and the advantage sums
+    for advantage normalisation (ppo_fused.py:119) -- produced and consumed by the batch
+    preparation kernels (g1_obs_prep, g1_gae, g1_runnorm_update, g1_adv_normalize),
   * the gradients, once per minibatch step (summed then divided by the world size).
 """
 import os
@@ -20,7 +21,8 @@ import torch
 import torch.nn as nn
 
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
-from g1env import AC, G1Env, RunNorm, evaluate, pack_weights  # noqa: E402
+from g1env import (AC, G1Env, RunNorm, adv_normalize_device, evaluate, gae_device, obs_prep_device,  # noqa: E402
+                   pack_weights, runnorm_update_device)
 
 
 # ---------------------------------------------------------------- distributed helpers
@@ -29,34 +31,33 @@ def _dist():
     return dist if dist.is_available() and dist.is_initialized() else None
 
 
-def global_moments(x):
-    """(mean, population var, count) of the rows of x over all ranks."""
+def allreduce_moments(*bufs):
+    """Sum the fp64 moment buffers of the batch preparation over ranks, in place, in one
+    all-reduce (obs moments [rows, sum o, sum o^2] and advantage moments [n, sum, sumsq])."""
     dist = _dist()
-    n = torch.tensor([float(x.shape[0])], dtype=torch.float64, device=x.device)
-    s = x.double().sum(0)
-    ss = (x.double() ** 2).sum(0)
-    if dist is not None:
-        buf = torch.cat([n, s, ss])
-        dist.all_reduce(buf)
-        n, s, ss = buf[:1], buf[1:1 + s.numel()], buf[1 + s.numel():]
-    cnt = float(n.item())
-    mean = s / cnt
-    var = (ss / cnt - mean ** 2).clamp_min(0.0)
-    return mean.to(x.dtype), var.to(x.dtype), cnt
+    if dist is None:
+        return bufs
+    flat = torch.cat([b.reshape(-1) for b in bufs])
+    dist.all_reduce(flat)
+    off = 0
+    for b in bufs:
+        b.copy_(flat[off:off + b.numel()].view_as(b))
+        off += b.numel()
+    return bufs
 
 
-def runnorm_update_global(norm, x):
-    """RunNorm.update (ppo.py:71-79) with the batch moments taken over all ranks."""
-    bm, bv, b = global_moments(x)
-    norm.update_from_moments(bm, bv, b)
-
-
-def normalize_advantages_global(adv):
-    """(adv - mean) / (std + 1e-8) with mean/std over all ranks (ppo_fused.py:119; torch.std
-    is the unbiased estimate)."""
-    m, v, n = global_moments(adv.reshape(-1, 1))
-    std = (v * n / max(n - 1.0, 1.0)).sqrt()
-    return (adv - m) / (std + 1e-8)
+def prepare_batch(norm, O, V, R, D, Vlast, fmean, fvar, gamma=0.99, lam=0.95):
+    """ppo_fused.py:104-119 on the GPU, straight from the rollout buffers:
+    nobs (frozen-stat renormalisation), RunNorm update from the raw observations, GAE, returns
+    and normalised advantages.  Only the moment buffers cross ranks."""
+    nobs, omom = obs_prep_device(O, fmean, fvar)
+    adv, ret, amom = gae_device(R, V, D, Vlast, gamma, lam)
+    allreduce_moments(omom, amom)
+    dist = _dist()
+    rows = (O.numel() // O.shape[-1]) * (dist.get_world_size() if dist is not None else 1)
+    runnorm_update_device(norm, omom, rows)
+    adv_normalize_device(adv, amom)
+    return nobs, adv, ret
 
 
 def allreduce_grads(params):
@@ -81,19 +82,6 @@ def broadcast_params(module):
         return
     for p in module.parameters():
         dist.broadcast(p.data, 0)
-
-
-def gae(R, V, D, Vlast, gamma=0.99, lam=0.95):
-    """GAE over the horizon (ppo_fused.py:108-116)."""
-    H = R.shape[0]
-    adv = torch.zeros_like(R)
-    g = torch.zeros_like(Vlast)
-    for t in reversed(range(H)):
-        nextv = Vlast if t == H - 1 else V[t + 1]
-        delta = R[t] + gamma * nextv * (1 - D[t]) - V[t]
-        g = delta + gamma * lam * (1 - D[t]) * g
-        adv[t] = g
-    return adv, adv + V
 
 
 def ppo_update(ac, opt, b_o, b_a, b_lp, b_adv, b_ret, epochs=5, mb=4, clip=0.2):
@@ -161,11 +149,9 @@ def main():
         W = pack_weights(ac).detach()
         env.rollout(H, W, fmean, fvar, O, A, LP, V, R, D, Vlast)
         with torch.no_grad():
-            nobs = torch.clamp((O - fmean) / torch.sqrt(fvar + 1e-8), -10.0, 10.0)
-            runnorm_update_global(norm, O.reshape(-1, O_dim))
-            adv, ret = gae(R, V, D, Vlast)
-            b_adv = normalize_advantages_global(adv.reshape(-1))
-        loss = ppo_update(ac, opt, nobs.reshape(-1, O_dim), A.reshape(-1, A_dim), LP.reshape(-1), b_adv, ret.reshape(-1))
+            nobs, b_adv, ret = prepare_batch(norm, O, V, R, D, Vlast, fmean, fvar)
+        loss = ppo_update(ac, opt, nobs.reshape(-1, O_dim), A.reshape(-1, A_dim), LP.reshape(-1), b_adv.reshape(-1),
+                          ret.reshape(-1))
         sps = world * (it + 1) * H * N / (time.time() - t0)
         ev = {"fwd_mean": float("nan"), "ep_len_mean": float("nan"), "fall_rate": float("nan"), "vx_mean": float("nan")}
         if rank == 0 and ((it % 25 == 0) or it == iters - 1):

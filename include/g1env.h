@@ -94,7 +94,10 @@ int g1_env_set_policy(void* h, int nh, const int* hidden, int activation);
 /* extension: policy_precision 1 runs the MLP on the tensor cores (tcgen05, bf16 weights and
  * activations, fp32 accumulation) as separate launches per control step, for wide policies
  * (widths multiple of 8, up to 1024); 0 = the fp32 in-kernel policy of
- * g1_env_set_policy.  Returns 0 on success. */
+ * g1_env_set_policy (computed with split-bf16 operands on the tensor cores -- fp32-class
+ * accuracy -- when
+ * every hidden width is a multiple of 16 in [16, 256], on FFMA otherwise); 2 = the fp32
+ * in-kernel policy always on FFMA.  Returns 0 on success. */
 int g1_env_set_policy_ex(void* h, int nh, const int* hidden, int activation, int policy_precision);
 
 /* extension: nonzero if a tensor-core wait of the bf16 policy path timed out since the last
@@ -127,6 +130,34 @@ int g1_qacc_batch(int n, const float* qpos, const float* qvel, const float* tau,
  * the large-policy rollout (reference counterpart: the per-world mlp_forward layers,
  * g1_env.cu:229-237, batched over worlds). */
 int g1_gemm_bf16_tc(int M, int N, int K, const void* X, int ldx, const void* W, const float* bias, int act, float* out);
+
+/* extension: the fp32 policy layer of the fused rollout as a standalone call -- out = act(X W^T
+ * + b) on the tensor cores with both operands split into three bf16 words (tcgen05 kind::f16,
+ * the six significant cross products, fp32 accumulation: fp32-class accuracy), rows <= 64,
+ * 16 <= N <= 256 with N % 16 == 0, K <= 256.  DEVICE pointers X
+ * [rows][K], W [N][K], b [N] or NULL, out [rows][N]; act 0 tanh, 1 ELU, -1 identity;
+ * synchronous; 0 on success.  Reference counterpart: one mlp_forward layer (g1_env.cu:229-237)
+ * for a block of worlds. */
+int g1_dense_bf16x3(int rows, int K, int N, const float* X, const float* W, const float* b, int act, float* out);
+
+/* extension: the trainer's batch preparation on the GPU, fed from the rollout buffers
+ * (reference counterpart: the Python GAE loop and torch reductions of scripts/ppo_fused.py:104-119
+ * and RunNorm.update, scripts/ppo.py:71-79).  DEVICE pointers, asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream), 0 on success.  Moment buffers are fp64 and
+ * zeroed by the producing call; several ranks may sum theirs (all-reduce) before the
+ * finalising calls.
+ *   g1_gae            adv/ret [H,N] from R/V/D [H,N], Vlast [N]; bit-identical to the torch loop;
+ *                     adv_mom[3] = {H*N, sum adv, sum adv^2}
+ *   g1_obs_prep       nobs = clamp((O - fmean)/sqrt(fvar + 1e-8), -10, 10) over O [rows][dim];
+ *                     obs_mom[1 + 2*dim] = {rows, sum o[dim], sum o^2[dim]} of the raw O
+ *   g1_adv_normalize  adv = (adv - mean)/(std + 1e-8), unbiased std, in place
+ *   g1_runnorm_update mean/var [dim] updated in place; count = the count before the update */
+int g1_gae(int H, int N, const float* R, const float* V, const float* D, const float* Vlast, double gamma, double lam,
+           float* adv, float* ret, double* adv_mom, void* stream);
+int g1_obs_prep(long long rows, int dim, const float* O, const float* fmean, const float* fvar, float* nobs,
+                double* obs_mom, void* stream);
+int g1_adv_normalize(long long n, float* adv, const double* adv_mom, void* stream);
+int g1_runnorm_update(int dim, float* mean, float* var, double count, const double* obs_mom, void* stream);
 
 #ifdef __cplusplus
 }

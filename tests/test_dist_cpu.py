@@ -17,18 +17,47 @@ def _free_port():
     return p
 
 
+def runnorm_from_moments(norm, mom):
+    """the arithmetic of k_runnorm (g1_ppo_prep.cuh) in torch fp64"""
+    dim = norm.mean.numel()
+    b = mom[0]
+    bm = mom[1:1 + dim] / b
+    bv = (mom[1 + dim:] / b - bm ** 2).clamp_min(0)
+    tot = norm.count + b
+    m0, v0 = norm.mean.double(), norm.var.double()
+    delta = bm - m0
+    norm.mean = (m0 + delta * b / tot).float()
+    norm.var = ((v0 * norm.count + bv * b + delta ** 2 * norm.count * b / tot) / tot).float()
+    norm.count = float(tot)
+
+
+def adv_norm_from_moments(adv, mom):
+    """the arithmetic of k_adv_norm (g1_ppo_prep.cuh)"""
+    n, mean = mom[0], mom[1] / mom[0]
+    std = ((mom[2] - n * mean * mean) / max(float(n) - 1.0, 1.0)).clamp_min(0).sqrt()
+    return (adv - mean.float()) / (std.float() + 1e-8)
+
+
 def _worker(rank, world, port, q):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_dist_cpu import adv_norm_from_moments, runnorm_from_moments
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import ppo_fused
     from g1env import AC, RunNorm
     g = torch.Generator().manual_seed(100 + rank)
     x = torch.randn(50 + 30 * rank, 100, generator=g) * (1 + rank)
     norm = RunNorm(100, "cpu")
-    ppo_fused.runnorm_update_global(norm, x)
     adv = torch.randn(40 + 10 * rank, generator=g)
-    nadv = ppo_fused.normalize_advantages_global(adv)
+    # the moment layouts g1_obs_prep / g1_gae produce, summed over ranks by the trainer
+    omom = torch.cat([torch.tensor([float(x.shape[0])], dtype=torch.float64), x.double().sum(0), (x.double() ** 2).sum(0)])
+    amom = torch.tensor([float(adv.numel()), adv.double().sum().item(), (adv.double() ** 2).sum().item()],
+                        dtype=torch.float64)
+    ppo_fused.allreduce_moments(omom, amom)
+    runnorm_from_moments(norm, omom)
+    nadv = adv_norm_from_moments(adv, amom)
     torch.manual_seed(0)
     ac = AC(100, 29)
     ppo_fused.broadcast_params(ac)

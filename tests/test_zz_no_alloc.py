@@ -2,7 +2,9 @@
 that cannot allocate on their hot path (e.g. a host framework that owns all device memory or
 has reserved its budget up front, or code running while a stream is being captured).  It
 keeps the repacked policy weights in a fixed device area of the library instead of an
-env-owned buffer.  Checked through the C-ABI against g1_rollout on two calls in a row.
+env-owned buffer, and computes the fp32 policy on the FFMA path (the tensor-core path of
+g1_rollout needs an env-owned weight image).  Checked through the C-ABI against g1_rollout
+with the same policy arithmetic (precision "fp32-ffma") on two calls in a row.
 
 This file is collected last on purpose: it runs after every other test, and it must also
 pass when run alone in a fresh process."""
@@ -28,6 +30,7 @@ def test_noalloc_rollout_matches_rollout_twice():
     var = torch.ones(100, device="cuda")
     ref = g1env.G1Env(N, 10, 8, seed=21)
     new = g1env.G1Env(N, 10, 8, seed=21)
+    ref.set_policy((256, 256), "tanh", precision="fp32-ffma")
     ref.reset()
     new.reset()
     for call in range(2):

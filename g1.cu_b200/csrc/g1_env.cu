@@ -437,6 +437,9 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
     for (int s = 0; s < P.S; ++s) {
         PROF_BEGIN();
         if (P.lockstep) substep_barrier();
+#ifdef G1_PROF
+        (void)*(volatile const float*)grp;  // bar.sync blocks lazily: make the wait land here
+#endif
         PROF_MARK(P_BAR);
         int ncon[GW];
         group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon);

@@ -573,12 +573,19 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
 // its contribution in hand[chain]; a body adds its children in descending child index.
 // u_b = x_d - S_d.pA_b parks in xy[d] between the sweeps; root->leaf a branch body leaves
 // its acceleration in fwd[slot].  `scratch`: SOLVE_SCRATCH floats of this lane.
-__device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, float* xy, float* scratch) {
+__device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, float* xy, float* scratch, int chains) {
     const float *S = fr + WL::S, *FU = fr + WL::FU, *FINVD = fr + WL::FINVD, *L6 = fr + WL::FL6;
     float* hand = scratch;
     float* fwd = scratch + 6 * 4;
-    // leaf -> root, chains last-to-first; the next body's index is fetched one body ahead
+    // leaf -> root, chains last-to-first; the next body's index is fetched one body ahead.
+    // Chains outside `chains` have a zero right-hand side: their pass would produce exact
+    // zeros, so it is skipped (their hand-off is zero).
     for (int c = T.nchain - 1; c >= 0; --c) {
+        if (!((chains >> c) & 1)) {
+#pragma unroll
+            for (int i = 0; i < 6; ++i) hand[6 * c + i] = 0.f;
+            continue;
+        }
         const int len = T.chain_len[c];
         float pa[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         int b = T.chain_body[c][len - 1], prev = -1;
@@ -782,8 +789,12 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     }
     __syncwarp();
     PROF_MARK(P_CSETUP);
-    if (lane < nb)
-        lane_solve(grp + B.wid[B.world_of(lane / 3)] * WFLOATS, T, MM + lane * MSTR, cw + CL::GRAM + lane * SOLVE_SCRATCH);
+    if (lane < nb) {
+        const int gc = lane / 3, x = B.world_of(gc);
+        const float* fr = grp + B.wid[x] * WFLOATS;
+        const int s = reinterpret_cast<const int*>(fr + WL::CON)[gc - B.coff[x]];
+        lane_solve(fr, T, MM + lane * MSTR, cw + CL::GRAM + lane * SOLVE_SCRATCH, T.foot_chains[s]);
+    }
     __syncwarp();
     PROF_MARK(P_SOLVE);
     // per contact: bb = e.qacc_smooth, e.qvel -> R, aref, b  (env_qacc.cuh:113-136, 188-191)
@@ -888,18 +899,24 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     const float ajj = lane < nefc_all ? AP[apidx(lane, lane)] : 1.f;
     const float inv = 1.f / ajj;
     const int lj = lane - r0;
+    // this lane's column of its world's block, in registers (off the row-to-row chain)
+    float acol[4 * MAXCON];
+#pragma unroll
+    for (int i = 0; i < 4 * MAXCON; ++i) acol[i] = i < nrow ? AP[apidx(r0 + i, lane)] : 0.f;
     for (int itr = 0; itr < opt.pgs_iters; ++itr) {
-        for (int i = 0; i < maxrow; ++i) {
+#pragma unroll
+        for (int i = 0; i < 4 * MAXCON; ++i) {
+            if (i >= maxrow) break;
             const bool live = i < nrow;
-            const float aji = live ? AP[apidx(r0 + i, lane)] : 0.f;
-            float delta = 0.f;
-            if (live && lj == i) {
-                const float ri = rj - ajj * fj;
-                float fn = -ri * inv;
-                fn = fn > 0.f ? fn : 0.f;
-                delta = fn - fj;
-                fj = fn;
-            }
+            const float aji = acol[i];
+            // every lane evaluates the update; the lane of row i of its world keeps it
+            // (branch-free: no divergence on the row-to-row chain)
+            const float ri = rj - ajj * fj;
+            float fn = -ri * inv;
+            fn = fn > 0.f ? fn : 0.f;
+            const bool mine = live && lj == i;
+            float delta = mine ? fn - fj : 0.f;
+            fj = mine ? fn : fj;
             delta = __shfl_sync(FULLMASK, delta, live ? r0 + i : lane);
             rj += aji * delta;
         }
@@ -925,11 +942,32 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     PROF_MARK(P_DQ);
 }
 
-// Full per-substep generalised acceleration for the GW worlds of the warp (qp, qv, tau
-// filled in each frame).  env_qacc.cuh:27-212.  qacc -> each frame's QACC; per-world
-// outputs for k_qacc through the optional arrays.
-__device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
-                           float* const* f_out, int* ncon_out, float* const* qs_out = nullptr) {
+// Contact batches of the group's worlds: greedy in slot order, at most MAXCON contacts per
+// batch (worlds without contacts are skipped).  Returns the number of batches.
+__device__ __forceinline__ int form_batches(const int* ncon, Batch* out) {
+    int nb = 0;
+    Batch B;
+    B.nw = 0;
+    B.coff[0] = 0;
+#pragma unroll 1
+    for (int w = 0; w <= GW; ++w) {
+        const bool flush = (w == GW) ? B.nw > 0 : (ncon[w] > 0 && B.coff[B.nw] + ncon[w] > MAXCON);
+        if (flush) {
+            out[nb++] = B;
+            B.nw = 0;
+        }
+        if (w < GW && ncon[w] > 0) {
+            B.wid[B.nw] = w;
+            B.coff[B.nw + 1] = B.coff[B.nw] + ncon[w];
+            ++B.nw;
+        }
+    }
+    return nb;
+}
+
+// Smooth dynamics and contact detection for the GW worlds of the warp; ncon per world.
+__device__ void group_smooth_detect(float* grp, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
+                                    int* ncon, float* const* qs_out = nullptr) {
     group_smooth(grp, T, lane, opt.bdt, bias_out);
     PROF_BEGIN();
     if (qs_out)
@@ -939,35 +977,37 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
         }
     group_detect(grp, T, lane);
     PROF_MARK(P_DETECT);
+#pragma unroll
+    for (int w = 0; w < GW; ++w) ncon[w] = reinterpret_cast<const int*>(grp + w * WFLOATS + WL::MISC)[0];
+}
+
+// Full per-substep generalised acceleration for the GW worlds of the warp (qp, qv, tau
+// filled in each frame), the warp solving its own contact batches.  env_qacc.cuh:27-212.
+// qacc -> each frame's QACC; per-world outputs for k_qacc through the optional arrays.
+__device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
+                           float* const* f_out, int* ncon_out, float* const* qs_out = nullptr) {
     int ncon[GW];
+    group_smooth_detect(grp, T, lane, opt, bias_out, ncon, qs_out);
 #pragma unroll
     for (int w = 0; w < GW; ++w) {
-        ncon[w] = reinterpret_cast<const int*>(grp + w * WFLOATS + WL::MISC)[0];
         if (ncon_out) ncon_out[w] = ncon[w];
         if (f_out && f_out[w] && ncon[w] == 0) f_out[w][lane] = 0.f;
     }
-    // greedy batches in slot order, at most MAXCON contacts each
-    Batch B;
-    B.nw = 0;
-    B.coff[0] = 0;
+    Batch bs[GW];
+    const int nb = form_batches(ncon, bs);
 #pragma unroll 1
-    for (int w = 0; w <= GW; ++w) {
-        const bool flush = (w == GW) ? B.nw > 0 : (ncon[w] > 0 && B.coff[B.nw] + ncon[w] > MAXCON);
-        if (flush) {
-            batch_contact(grp, cw, T, lane, opt, B);
-            if (f_out)
-                for (int x = 0; x < B.nw; ++x)
-                    if (f_out[B.wid[x]]) {
-                        const int n4 = 4 * (B.coff[x + 1] - B.coff[x]);
-                        f_out[B.wid[x]][lane] = lane < n4 ? cw[CL::FF + 4 * B.coff[x] + lane] : 0.f;
-                    }
-            B.nw = 0;
-        }
-        if (w < GW && ncon[w] > 0) {
-            B.wid[B.nw] = w;
-            B.coff[B.nw + 1] = B.coff[B.nw] + ncon[w];
-            ++B.nw;
-        }
+    for (int i = 0; i < nb; ++i) {
+        const Batch& B = bs[i];
+#ifdef G1_PROF
+        if (lane == 0) atomicAdd(&g_prof[23 + B.coff[B.nw]], 1ull);  // batches by contact count 1..8
+#endif
+        batch_contact(grp, cw, T, lane, opt, B);
+        if (f_out)
+            for (int x = 0; x < B.nw; ++x)
+                if (f_out[B.wid[x]]) {
+                    const int n4 = 4 * (B.coff[x + 1] - B.coff[x]);
+                    f_out[B.wid[x]][lane] = lane < n4 ? cw[CL::FF + 4 * B.coff[x] + lane] : 0.f;
+                }
     }
 }
 

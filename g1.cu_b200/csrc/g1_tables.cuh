@@ -56,6 +56,7 @@ struct alignas(16) G1Tables {
     int child_list[G1_NB];
     int foot_ndof[G1_NFOOT_];
     unsigned char foot_dofs[G1_NFOOT_][G1_CDS];
+    int foot_chains[G1_NFOOT_];  // bit c: chain c holds an ancestor of the sphere's body
     // chain decomposition of the hinge bodies (root->leaf order inside a chain); lane l of
     // a warp walks chain l.  A chain starts at a child of the floating base or of a branch
     // body; f1_start is the sweep step of its head (its parent is done by then).
@@ -225,6 +226,12 @@ static inline void g1_build_tables(G1Tables* T) {
             for (int a = G1M_BODY_DOFADR[b]; a < G1M_BODY_DOFADR[b] + G1M_BODY_DOFNUM[b]; ++a)
                 if (k < G1_CDS) T->foot_dofs[s][k++] = (unsigned char)a;
         T->foot_ndof[s] = k;
+        int mask = 0;
+        for (int b = G1M_FOOT_BODY[s]; b >= 2; b = G1M_BODY_PARENT[b])
+            for (int c = 0; c < T->nchain; ++c)
+                for (int q = 0; q < T->chain_len[c]; ++q)
+                    if (T->chain_body[c][q] == b) mask |= 1 << c;
+        T->foot_chains[s] = mask;
     }
 }
 #endif

@@ -61,7 +61,7 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms during the timed region."""
     Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -72,7 +72,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -242,7 +242,7 @@ def profile_case(h):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-ref-kernel", action="store_true")
@@ -351,9 +351,10 @@ def main():
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": 2 * args.steps,
                 "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
-                             "frac": achieved / fp32_peak, "traffic": 145e6,
-                             "traffic_source": "ncu dram__bytes_read+write of one H=2 launch (9.09 MB), scaled x16 to H=32 (profiles/k_g1_rollout_n8192_h32.md)",
-                             "peak_source": f"nominal FP32 FMA rate: {sm_count} SMs x 128 lanes x 2 x {clk:.0f} MHz "
+                             "frac": achieved / fp32_peak, "traffic": 120.7e6,
+                             "traffic_source": "ncu dram__bytes_read+write of one H=2 launch (7.54 MB), scaled x16 to H=32 (profiles/k_g1_rollout_n8192_h32.md)",
+                             "peak_source": f"nominal FP32 FMA rate: {sm_count} SMs x 128 lanes x 2 x {clk:.0f} MHz; the policy "
+                                            f"MLP (counted at its algorithmic fp32 FLOPs) runs on the tensor cores "
                                             f"(MEASURED_PEAKS.json has no FP32 figure; its hbm/bf16 peaks are {peak_src})",
                              "flop_per_substep": flop_sub, "ncon_hist": hist.tolist()},
                 "clocks": ck,

@@ -10,8 +10,13 @@ Sources:
   * the reference's physics headers compiled for the host (oracle/_ref, built by
     oracle/build_oracle.py): FK + env_qacc outputs on seeded states in fp32 (the
     reference's arithmetic) and fp64, at mu = 0.6 and mu = 1.0.
+  * the reference's trained finish-line walker (models/ppo_ckpt/finish_best.pt, a torch
+    checkpoint {model: AC state_dict, obs_mean, obs_var}) as plain arrays in
+    finish_policy.npz, with the playback result the reference documents for it
+    (DEVLOG.md:421-422, scripts/play_finish.py: 256 worlds, deterministic actions, <= 480
+    control steps -> 256/256 reach x = 5 m).
 
-    python tests/golden/make_golden.py [reference-root]
+    python tests/golden/make_golden.py [reference-root] [--policy-only]
 """
 import os
 import sys
@@ -23,6 +28,16 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
 FOOT_GEOMS = {15, 16, 17, 18, 30, 31, 32, 33}
+
+
+def export_finish_policy(ref_root):
+    import torch
+    ck = torch.load(os.path.join(ref_root, "models", "ppo_ckpt", "finish_best.pt"), map_location="cpu")
+    arrays = {"param." + k: v.numpy().astype(np.float32) for k, v in ck["model"].items()}
+    np.savez_compressed(os.path.join(HERE, "finish_policy.npz"), obs_mean=ck["obs_mean"].numpy().astype(np.float32),
+                        obs_var=ck["obs_var"].numpy().astype(np.float32), playback_worlds=np.int32(256),
+                        playback_max_steps=np.int32(480), playback_reached=np.int32(256), x_fin=np.float32(5.0),
+                        **arrays)
 
 
 def main(ref_root):
@@ -77,10 +92,16 @@ def main(ref_root):
     np.savez_compressed(os.path.join(HERE, "ref_config1.npz"), qpos=qp1.astype(np.float32), qvel=qv1.astype(np.float32),
                         qacc_f32=r32.qacc(qp1.astype(np.float32), qv1.astype(np.float32), None, bdt, 8),
                         qacc_f64=r64.qacc(qp1, qv1, None, bdt, 8))
+    export_finish_policy(ref_root)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = args[0] if args else "/root/reference"
+    if "--policy-only" in sys.argv:
+        export_finish_policy(root)
+    else:
+        main(root)

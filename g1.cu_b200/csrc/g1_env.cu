@@ -384,6 +384,7 @@ __device__ __forceinline__ void substep_barrier() { asm volatile("bar.sync 1, %0
 __device__ void group_control_step(const Params& P, const G1Tables& T, float* grp, float* cw, const int* wid, int nvalid,
                                    const float* acts_base, uint64_t tick, float* r_out, float* d_out) {
     const int lane = threadIdx.x & 31;
+    PROF_BEGIN();
     // slot w < nvalid holds world wid[w]; its actions are acts_base[wid[w]] (null = zero)
     // load state
     for (int it = lane; it < GW * NQ; it += 32) {
@@ -410,6 +411,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
     for (int w = 0; w < GW; ++w) bdt_all[w] = T.bdt;
     QaccOpts opt;
     opt.pgs_iters = P.pgs; opt.mu = P.mu; opt.bdt = bdt_all;
+    PROF_MARK(P_CS_LOAD);
     // PD torque, clamped to the actuator range, and |tau qd| accumulated into the energy
     // actuator by actuator in index order (g1_env.cu:143-152).  The torque of substep s + 1 is
     // computed right after substep s integrates (same values; it keeps this small piece of code
@@ -461,6 +463,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
         }
     }
     // reward / termination per world (g1_env.cu:164-197), lane w
+    PROF_RESTART();
     int d_flag = 0;
     if (lane < nvalid) {
         const int w = lane, gw = wid[w];
@@ -496,6 +499,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
     }
     unsigned dmask = __ballot_sync(FULLMASK, d_flag != 0);
     __syncwarp();
+    PROF_MARK(P_CS_REWARD);
     // auto-reset (g1_env.cu:202-210), store state and previous action
     for (int it = lane; it < GW * NQ; it += 32) {
         const int w = it / NQ, i = it % NQ;
@@ -524,6 +528,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
         if (w < nvalid) P.qv[(size_t)wid[w] * NV + i] = ((dmask >> w) & 1u) ? 0.f : grp[w * WFLOATS + WL::QV + i];
     }
     __syncwarp();
+    PROF_MARK(P_CS_STORE);
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -554,6 +559,9 @@ __device__ __forceinline__ void load_tables(float* smem) {
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
+#ifdef G1_PROF
+    const long long t_kernel0 = clock64();
+#endif
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     const SmemPlan plan = smem_plan();
@@ -589,6 +597,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
         // similar contact load.  Warp takes groups warp, warp + NWARPS, ...; a warp with no
         // group in a round still passes the substep barriers.
         const int ngroups = (nbw + GW - 1) / GW;
+        PROF_BEGIN();
         if (warp == 0) {
             int v0 = -1, v1 = -1;  // this lane's two worlds (nbw <= 64)
             if (lane < nbw) v0 = P.ncon_last ? P.ncon_last[wbeg + lane] : 0;
@@ -603,6 +612,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
             }
         }
         __syncthreads();
+        PROF_MARK(P_SORT);
         for (int round = 0; round < nrounds; ++round) {
             const int g = warp + round * NWARPS;
             int wid[GW];
@@ -657,6 +667,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
     }
     if (P.mode == MODE_ROLLOUT && !P.ext_policy) policy_phase(P, T, frames, wbeg, nbw, 0, true, tfs);
     if (use_tf) g1tc::tf_release(reinterpret_cast<g1tc::TfShared*>(tfs));
+#ifdef G1_PROF
+    if (lane == 0) atomicAdd(&g_prof[P_TOTAL], (unsigned long long)(clock64() - t_kernel0));
+#endif
 }
 // Per-state FK + generalised acceleration (the reference's test_envqacc.cu harness
 // semantics, with caller states): a warp takes GW states at a time.
@@ -1459,11 +1472,11 @@ int g1_qacc_batch(int n, const float* qpos, const float* qvel, const float* tau,
 
 #ifdef G1_PROF
 // profiling builds only (-DG1_PROF, not part of the shipped ABI): per-phase warp cycles
-// since the last call.
+// since the last call (64 counters: phases from 0, contact batches by size at 48..55).
 int g1_prof_read(unsigned long long* out) {
     CKR(cudaDeviceSynchronize(), -1);
-    CKR(cudaMemcpyFromSymbol(out, g_prof, sizeof(unsigned long long) * 32), -1);
-    unsigned long long z[32] = {0};
+    CKR(cudaMemcpyFromSymbol(out, g_prof, sizeof(unsigned long long) * 64), -1);
+    unsigned long long z[64] = {0};
     CKR(cudaMemcpyToSymbol(g_prof, z, sizeof z), -1);
     return 0;
 }

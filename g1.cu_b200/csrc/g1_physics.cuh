@@ -181,8 +181,9 @@ __device__ __forceinline__ int apidx(int i, int j) {  // packed upper triangle o
 
 // ------------------------------------------------------------------ profiling (G1_PROF builds)
 #ifdef G1_PROF
-__device__ unsigned long long g_prof[32];
+__device__ unsigned long long g_prof[64];
 #define PROF_BEGIN() long long _pt = clock64();
+#define PROF_RESTART() _pt = clock64();
 #define PROF_MARK(i)                                                                          \
     do {                                                                                      \
         long long _n = clock64();                                                             \
@@ -191,9 +192,10 @@ __device__ unsigned long long g_prof[32];
     } while (0)
 #else
 #define PROF_BEGIN()
+#define PROF_RESTART()
 #define PROF_MARK(i) do { } while (0)
 #endif
-enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_NPHASE };
+enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_CS_LOAD, P_CS_REWARD, P_CS_STORE, P_SORT, P_TOTAL, P_NPHASE };
 
 // pyramid coefficients d_k = DC[k] of the 3-basis (env_qacc.cuh:98-100,154-155)
 __device__ __forceinline__ float dcoef(int k, int a) {
@@ -999,7 +1001,7 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
     for (int i = 0; i < nb; ++i) {
         const Batch& B = bs[i];
 #ifdef G1_PROF
-        if (lane == 0) atomicAdd(&g_prof[23 + B.coff[B.nw]], 1ull);  // batches by contact count 1..8
+        if (lane == 0) atomicAdd(&g_prof[47 + B.coff[B.nw]], 1ull);  // batches by contact count 1..8
 #endif
         batch_contact(grp, cw, T, lane, opt, B);
         if (f_out)

@@ -20,7 +20,8 @@ sys.path.insert(0, HERE)
 LIB = os.path.join(HERE, "libg1env_prof.so")
 NAMES = ["policy", "F1", "B1", "base", "F2", "contact_setup", "back_solves", "gram", "pgs", "dq", "pd_torque",
          "end_of_step_wait", "integrate", "detect", "mlp_layer0", "sampling", "mlp_layer1", "mlp_head",
-         "substep_barrier_wait", "energy", "mlp_mma_wait", "mlp_epilogue"]
+         "substep_barrier_wait", "energy", "mlp_mma_wait", "mlp_epilogue", "step_state_load", "reward_done",
+         "state_store_reset", "contact_sort", "kernel_total"]
 
 
 def build():
@@ -49,13 +50,17 @@ def main():
     z = lambda *s: torch.zeros(*s, device="cuda")
     bufs = [z(H, N, 100), z(H, N, 29), z(H, N), z(H, N), z(H, N), z(H, N), z(N)]
     env.rollout(H, W, mean, var, *bufs)
-    out = (ctypes.c_ulonglong * 32)()
+    out = (ctypes.c_ulonglong * 64)()
     lib.g1_prof_read(out)  # clear
     env.rollout(H, W, mean, var, *bufs)
     lib.g1_prof_read(out)
     nwarps = torch.cuda.get_device_properties(0).multi_processor_count * 7
-    per = {n: round(out[i] / nwarps / H) for i, n in enumerate(NAMES)}
-    batches = [round(out[23 + c] / H / (nwarps // 7), 2) for c in range(1, 9)]
+    nw_live = ((N + 55) // 56) * 7  # warps of the launched CTAs (56-world blocks)
+    per = {n: round(out[i] / nw_live / H) for i, n in enumerate(NAMES)}
+    per["unattributed"] = per["kernel_total"] - sum(v for k, v in per.items()
+                                                    if k not in ("kernel_total", "mlp_layer0", "mlp_layer1", "mlp_head",
+                                                                 "sampling", "mlp_mma_wait", "mlp_epilogue"))
+    batches = [round(out[47 + c] / H / (nw_live // 7), 2) for c in range(1, 9)]
     print(json.dumps({"N": N, "H": H, "cycles_per_warp_per_control_step": per,
                       "contact_batches_per_cta_per_control_step_by_size_1_to_8": batches}))
     env.close()

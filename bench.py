@@ -239,6 +239,69 @@ def profile_case(h):
     print("profile case done")
 
 
+def other_configs(dev):
+    """Informational timings of BASELINE configs 1 and 3 on this GPU (CUDA events, L2 flushed
+    between timed calls); the headline metric is config 2."""
+    import torch
+    import g1env
+    out = {}
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def timed(fn, reps):
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            ts.append((e0, e1))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ts) / reps
+
+    # config 1: physics only, N = 8192, mu = 1.0, 32 control steps x 10 substeps, a constant
+    # action U(-1,1) per world through the PD-target path; state = the reset pose with base
+    # height U(0.75, 0.8) m and qvel ~ N(0, 0.5)
+    rng = np.random.default_rng(11)
+    N1, K1 = 8192, 32
+    env = g1env.G1Env(N1, S, PGS, seed=11, device=dev.index, mu=1.0)
+    env.reset()
+    st = env.get_state()
+    qp, qv = st[0].copy(), rng.normal(0, 0.5, (N1, 35)).astype(np.float32)
+    qp[:, 2] = rng.uniform(0.75, 0.8, N1)
+    act = torch.tensor(rng.uniform(-1, 1, (N1, 29)).astype(np.float32), device=dev)
+
+    def c1():
+        env.set_state(qp, qv, st[2], st[3], st[4])
+        env.phys_actions(K1, act)
+    c1()
+    torch.cuda.synchronize()
+    ms1 = timed(c1, 3)
+    env.close()
+    out["config1"] = {"value": N1 * K1 * S / (ms1 * 1e-3), "unit": "substeps/s", "ms": ms1,
+                      "what": "physics only, N=8192, mu=1.0, 32 control steps x 10 substeps, constant U(-1,1) "
+                              "action per world (state upload included in the timed call)"}
+    # config 3: N = 32768, H = 32, policy 100-1024-1024-512-29 ELU on the tensor cores (bf16)
+    N3, H3 = 32768, 32
+    env = g1env.G1Env(N3, S, PGS, seed=3, device=dev.index)
+    env.set_policy((1024, 1024, 512), "elu", precision="bf16")
+    env.reset()
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (1024, 1024, 512), "elu"), seed=0).to(dev)
+    W = g1env.pack_weights(ac).detach().contiguous()
+    mean, var = torch.zeros(100, device=dev), torch.ones(100, device=dev)
+    z = lambda *sh: torch.zeros(*sh, device=dev)
+    bufs = [z(H3, N3, 100), z(H3, N3, 29), z(H3, N3), z(H3, N3), z(H3, N3), z(H3, N3), z(N3)]
+    env.rollout(H3, W, mean, var, *bufs)
+    torch.cuda.synchronize()
+    ms3 = timed(lambda: env.rollout(H3, W, mean, var, *bufs), 2)
+    if env.tc_status():
+        raise RuntimeError("tensor-core wait timed out in the config-3 rollout")
+    env.close()
+    out["config3"] = {"value": N3 * H3 * S / (ms3 * 1e-3), "unit": "substeps/s", "ms": ms3,
+                      "what": "fused rollout N=32768, H=32, S=10, policy 100-1024-1024-512-29 ELU, bf16 on tcgen05"}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -246,6 +309,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-ref-kernel", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true")
     ap.add_argument("--profile-case", type=int, default=0, metavar="H",
                     help="run two H-step rollouts of the config-2 worlds and exit (small case for ncu captures)")
     args = ap.parse_args()
@@ -341,6 +405,12 @@ def main():
         except Exception:  # the reference kernel is a comparison only
             ref_ms = None
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
+    others = None
+    if rank == 0 and world == 1 and not args.no_other_configs:
+        try:
+            others = other_configs(dev)
+        except Exception as e:  # informational only
+            others = {"error": str(e)[:200]}
     env.close()
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "substeps/s", "n_gpus": world, "steps": args.steps,
@@ -363,6 +433,8 @@ def main():
                     "what": "reference k_rollout (src/g1_env.cu) built for sm_100a, same N/H/S, 1 GPU"}}
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if others is not None:
+            line["other_configs"] = others
         print(json.dumps(line), flush=True)
     barrier(world)
     if world > 1:

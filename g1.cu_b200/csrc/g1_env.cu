@@ -120,6 +120,7 @@ struct Params {
     long long tf_woff[MAX_HIDDEN + 1];
     int tf_boff[MAX_HIDDEN + 1], tf_lsoff;
     int* tf_err;
+    int o_vec;  // O is 16-byte aligned: 128-bit observation stores
 };
 
 // ------------------------------------------------------------------ observations
@@ -271,18 +272,30 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
             const float* qp = P.qp + (size_t)gw * NQ;
             const float* qv = P.qv + (size_t)gw * NV;
             const float* pa = P.pa + (size_t)gw * NU;
-            float v[8];
+            float v[8], o[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int i = k0 + j;
                 float z = 0.f;
+                o[j] = 0.f;
                 if (i < OBS_DIM) {
-                    const float o = obs_elem(i, qp, qv, pa, T);
-                    if (!final_value) P.O[((size_t)t * P.N + gw) * OBS_DIM + i] = o;
-                    z = (o - P.mean[i]) / sqrtf(P.var[i] + 1e-8f);
+                    o[j] = obs_elem(i, qp, qv, pa, T);
+                    z = (o[j] - P.mean[i]) / sqrtf(P.var[i] + 1e-8f);
                     if (z < -10.f) z = -10.f; else if (z > 10.f) z = 10.f;
                 }
                 v[j] = z;
+            }
+            if (!final_value && k0 < OBS_DIM) {
+                float* row = P.O + ((size_t)t * P.N + gw) * OBS_DIM + k0;
+                if (P.o_vec) {  // raw obs: 16-byte stores (rows are 400 B; O is 16-byte aligned)
+                    float4* dst = reinterpret_cast<float4*>(row);
+                    dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+                    if (k0 + 8 <= OBS_DIM) dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (k0 + j < OBS_DIM) row[j] = o[j];
+                }
             }
             g1tc::tf_store8(tf_A, w, k0, v);
         }
@@ -629,7 +642,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
                 continue;
             }
             const float* acts = P.mode == MODE_ROLLOUT ? P.A + (size_t)trow * P.N * ACT_DIM
-                              : (P.mode == MODE_STEP ? P.act_in : nullptr);
+                              : P.act_in;  // MODE_STEP: this step's actions; MODE_PHYS: constant actions (may be null = zero)
             float r[GW], d[GW];
             group_control_step(P, T, grp, cw, wid, nvalid, acts, tick, r, d);
             int my_w = 0;
@@ -1062,6 +1075,7 @@ static void rollout_tc(EnvState* E, int H, const float* W, const float* mean, co
     P.mode = MODE_ROLLOUT; P.H = 1; P.ext_policy = 1;
     P.mean = mean; P.var = var;
     P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
+    P.o_vec = ((uintptr_t)O & 15) == 0;
     const dim3 oblk(32, 8);
     const int ogrid = (N + 7) / 8;
     auto policy = [&](int row, uint64_t tick) -> bool {
@@ -1348,6 +1362,7 @@ void g1_rollout(void* h, int H, const float* W, const float* mean, const float* 
     P.mode = MODE_ROLLOUT; P.H = H;
     P.WT = E->WT; P.mean = mean; P.var = var;
     P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
+    P.o_vec = ((uintptr_t)O & 15) == 0;
     if (launch_g1(E, P)) E->tick += (uint64_t)H;
 }
 
@@ -1376,6 +1391,7 @@ void g1_rollout_noalloc(void* h, int H, const float* W, const float* mean, const
     P.mode = MODE_ROLLOUT; P.H = H;
     P.WT = wt; P.mean = mean; P.var = var;
     P.O = O; P.A = A; P.LP = LP; P.V = V; P.R = R; P.D = D; P.Vlast = Vlast;
+    P.o_vec = ((uintptr_t)O & 15) == 0;
     if (launch_g1(E, P)) E->tick += (uint64_t)H;
 }
 
@@ -1388,6 +1404,17 @@ void g1_env_bench_phys(void* h, int K) {
     if (!launch_g1(E, P)) return;
     E->tick += (uint64_t)K;
     CKR(cudaStreamSynchronize(E->stream), );
+}
+
+// extension: K control steps of physics only with a constant action per
+// world, act = DEVICE [N, 29] (null = zero, as g1_env_bench_phys); asynchronous on the env
+// stream.  The actions go through the same PD-target path as the rollout's.
+void g1_env_phys_actions(void* h, int K, const float* act) {
+    EnvState* E = (EnvState*)h;
+    if (K <= 0) return;
+    Params P = base_params(E);
+    P.mode = MODE_PHYS; P.K = K; P.act_in = act;
+    if (launch_g1(E, P)) E->tick += (uint64_t)K;
 }
 
 // Asynchronous variant of g1_env_bench_phys (for timing with events on the env stream).

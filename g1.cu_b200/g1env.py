@@ -35,6 +35,7 @@ SIGNATURES = {
     "g1_rollout_noalloc": (None, [_vp, ctypes.c_int] + [_vp] * 10),
     "g1_env_bench_phys": (None, [_vp, ctypes.c_int]),
     "g1_env_phys_async": (None, [_vp, ctypes.c_int]),
+    "g1_env_phys_actions": (None, [_vp, ctypes.c_int, _vp]),
     "g1_env_qpos": (None, [_vp, _fp]),
     "g1_env_qpos_all": (None, [_vp, _fp]),
     "g1_env_obs_dim": (ctypes.c_int, []),
@@ -174,6 +175,11 @@ class G1Env:
 
     def phys_async(self, K):
         _lib.g1_env_phys_async(self.h, K); _check()
+
+    def phys_actions(self, K, act=None):
+        """g1_env_phys_actions: K control steps of physics with a constant action per world
+        (act: CUDA tensor [N, 29], None = zero), asynchronous."""
+        _lib.g1_env_phys_actions(self.h, K, _dp(act.contiguous() if act is not None else None)); _check()
 
     def get_state(self):
         N = self.N

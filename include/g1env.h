@@ -68,6 +68,11 @@ void g1_env_bench_phys(void* h, int K);
 /* extension: asynchronous g1_env_bench_phys (timing with events on the env stream). */
 void g1_env_phys_async(void* h, int K);
 
+/* extension: K control steps of physics only with a constant action per
+ * world, act = DEVICE [N, 29] (NULL = zero actions, as g1_env_bench_phys); asynchronous on the
+ * env's stream.  The actions go through the rollout's PD-target path (g1_env.cu:123-152). */
+void g1_env_phys_actions(void* h, int K, const float* act);
+
 /* replaces g1_env_qpos / g1_env_qpos_all, g1_env.cu:457-467 (HOST out [36] / [N*36]). */
 void g1_env_qpos(void* h, float* out);
 void g1_env_qpos_all(void* h, float* out);

@@ -240,3 +240,28 @@ def test_errors_are_reported_not_fatal(g1):
     assert not h
     assert lib.g1_env_last_error() is not None
     lib.g1_env_clear_error()
+
+
+def test_config1_constant_actions_vs_oracle(g1):
+    """BASELINE config 1 (physics only, mu = 1.0, constant per-world actions through the
+    PD-target path) against the fp32 oracle's host-loop steps with the same actions."""
+    from oracle.oracle import Oracle, OracleEnv, config0_states
+    N, K = 64, 3
+    qp, qv = config0_states(N, seed=21)
+    qp, qv = qp.astype(np.float32), qv.astype(np.float32)
+    act = np.random.default_rng(3).uniform(-1, 1, (N, 29)).astype(np.float32)
+    env = g1.G1Env(N, 10, 8, seed=5, mu=1.0)
+    env.reset()
+    st = env.get_state()
+    env.set_state(qp, qv, st[2], st[3], st[4])
+    oenv = OracleEnv(Oracle("f32"), N, 10, 8, seed=5, mu=1.0)
+    oenv.set_state(qp, qv, st[2], st[3], tick=st[4])
+    env.phys_actions(K, torch.tensor(act).cuda())
+    torch.cuda.synchronize()
+    for _ in range(K):
+        oenv.step(act)
+    gs, os_ = env.get_state(), oenv.get_state()
+    assert np.array_equal(gs[3], os_[3]) and gs[4] == os_[4] == st[4] + K   # episode counters, tick
+    assert np.abs(gs[0] - os_[0]).max() < 1e-3
+    assert np.abs(gs[2] - os_[2]).max() == 0.0   # previous action stored exactly
+    env.close()

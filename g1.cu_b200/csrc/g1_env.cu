@@ -766,11 +766,13 @@ __global__ void k_obs_norm(Params P, int row, __nv_bfloat16* Xb) {
 
 // Gaussian actions and log-probabilities from the head outputs HD [N][32] (29 means, value)
 // (g1_env.cu:308-318); row < 0: only the bootstrap value -> Vlast
-__global__ void k_sample(Params P, int row, const float* HD, const float* ls, uint64_t tick) {
+// HV: the [N][32] head output whose column 29 is the value (HD itself for the shared trunk)
+__global__ void k_sample(Params P, int row, const float* HD, const float* HV, const float* ls, uint64_t tick) {
     const int w = blockIdx.x * blockDim.x + threadIdx.x;
     if (w >= P.N) return;
     const float* hd = HD + (size_t)w * 32;
-    if (row < 0) { P.Vlast[w] = hd[29]; return; }
+    const float val = HV[(size_t)w * 32 + 29];
+    if (row < 0) { P.Vlast[w] = val; return; }
     const float LOG2PI = 1.8378770664093453f;
     const size_t sb = (size_t)row * P.N + w;
     float lps = 0.f;
@@ -782,7 +784,7 @@ __global__ void k_sample(Params P, int row, const float* HD, const float* ls, ui
         P.A[sb * ACT_DIM + i] = a;
     }
     P.LP[sb] = lps;
-    P.V[sb] = hd[29];
+    P.V[sb] = val;
 }
 
 // torch-ordered fp32 weights (ppo_fused.py:35-44) -> bf16 [out][in] per layer (layer 0's
@@ -794,6 +796,7 @@ struct RepackPlan {
     long long srcW[MAX_HIDDEN + 1], srcB[MAX_HIDDEN + 1], dstW[MAX_HIDDEN + 1], dstB[MAX_HIDDEN + 1];
     int nin[MAX_HIDDEN + 1], nout[MAX_HIDDEN + 1], ninp[MAX_HIDDEN + 1];
     long long srcLS;
+    int novalue;  // separate value network: the policy head's value row is zero
 };
 // fp32 policy -> split-bf16 chunk images for the in-kernel tensor-core MLP (g1_mlp_tc.cuh,
 // tf_layer): per layer, ceil(nin/16) chunks of [w1 | w2 | w3] in the canonical K-major
@@ -845,6 +848,32 @@ __global__ void k_tf_image_layer(const float* W, const float* b, int K, int N, _
     for (size_t e = tid; e < (size_t)N; e += nth) bias[e] = b ? b[e] : 0.f;
 }
 
+// separate value network: per hidden layer W, b, then the output row
+// (1 x last) placed as row 29 of a 32-row head (so the value lands where the shared-trunk
+// head puts it); layer 0's inputs padded to XK
+__global__ void k_repack_bf16_value(const float* W, __nv_bfloat16* Wb, float* Bf, RepackPlan R) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
+    for (int l = 0; l <= R.nl; ++l) {
+        const bool head = l == R.nl;
+        const int nin = R.nin[l], ninp = R.ninp[l], nout = head ? 32 : R.nout[l];
+        for (size_t e = tid; e < (size_t)nout * ninp; e += nth) {
+            const int o = (int)(e / ninp), i = (int)(e % ninp);
+            float v = 0.f;
+            if (i < nin) {
+                if (!head) v = W[R.srcW[l] + (size_t)o * nin + i];
+                else if (o == ACT_DIM) v = W[R.srcW[l] + i];
+            }
+            Wb[R.dstW[l] + e] = __float2bfloat16(v);
+        }
+        for (size_t e = tid; e < (size_t)nout; e += nth) {
+            float b = 0.f;
+            if (!head) b = W[R.srcB[l] + e];
+            else if (e == ACT_DIM) b = W[R.srcB[l]];
+            Bf[R.dstB[l] + e] = b;
+        }
+    }
+}
+
 __global__ void k_repack_bf16(const float* W, __nv_bfloat16* Wb, float* Bf, float* LS, RepackPlan R) {
     const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
     for (int l = 0; l <= R.nl; ++l) {
@@ -856,7 +885,7 @@ __global__ void k_repack_bf16(const float* W, __nv_bfloat16* Wb, float* Bf, floa
             if (i < nin) {
                 if (!head) v = W[R.srcW[l] + (size_t)o * nin + i];
                 else if (o < ACT_DIM) v = W[R.srcW[l] + (size_t)o * nin + i];
-                else if (o == ACT_DIM) v = W[R.srcW[l] + (size_t)ACT_DIM * nin + ACT_DIM + i];  // Wv after bmu
+                else if (o == ACT_DIM && !R.novalue) v = W[R.srcW[l] + (size_t)ACT_DIM * nin + ACT_DIM + i];  // Wv after bmu
             }
             Wb[R.dstW[l] + e] = __float2bfloat16(v);
         }
@@ -864,7 +893,7 @@ __global__ void k_repack_bf16(const float* W, __nv_bfloat16* Wb, float* Bf, floa
             float b = 0.f;
             if (!head) b = W[R.srcB[l] + e];
             else if (e < ACT_DIM) b = W[R.srcB[l] + e];
-            else if (e == ACT_DIM) b = W[R.srcB[l] + ACT_DIM + nin];  // bv
+            else if (e == ACT_DIM && !R.novalue) b = W[R.srcB[l] + ACT_DIM + nin];  // bv
             Bf[R.dstB[l] + e] = b;
         }
     }
@@ -948,6 +977,10 @@ struct EnvState {
     float *Bf, *LS, *HD;
     int* derr;
     size_t tc_N, tc_w, tc_wb;
+    int vnh, vhid[MAX_HIDDEN];          // separate value network (bf16 path), vnh = 0: shared trunk
+    __nv_bfloat16* Wvb;
+    float *Bvf, *HDv;
+    size_t tc_wvb, tc_hdv;
     uint8_t* tf_img;                    // fp32 policy on the tensor cores: chunk images + biases
     size_t tf_cap;
     int ffma_only;                      // 1: keep the fp32 policy on the FFMA path
@@ -1050,7 +1083,38 @@ static void rollout_tc(EnvState* E, int H, const float* W, const float* mean, co
         db += no;
         if (!head) { src += (long long)nin * no + no; nin = no; }
     }
-    RP.srcLS = src + (long long)ACT_DIM * nin + ACT_DIM + nin + 1;
+    // separate value network: the policy part ends [.. Wmu, bmu, log_std], the value
+    // network's layers and its 1-row output follow (g1env.pack_weights with value_hidden)
+    const bool vnet = E->vnh > 0;
+    RP.novalue = vnet;
+    RP.srcLS = vnet ? src + (long long)ACT_DIM * nin + ACT_DIM : src + (long long)ACT_DIM * nin + ACT_DIM + nin + 1;
+    RepackPlan VP;
+    memset(&VP, 0, sizeof VP);
+    long long vdw = 0, vdb = 0;
+    if (vnet) {
+        long long vs = RP.srcLS + ACT_DIM;
+        int vin = OBS_DIM;
+        VP.nl = E->vnh;
+        for (int l = 0; l <= E->vnh; ++l) {
+            const bool head = l == E->vnh;
+            const int no = head ? 32 : E->vhid[l];
+            VP.srcW[l] = vs; VP.nin[l] = vin; VP.ninp[l] = l == 0 ? XK : vin; VP.nout[l] = no;
+            VP.srcB[l] = vs + (long long)(head ? 1 : no) * vin;
+            VP.dstW[l] = vdw; VP.dstB[l] = vdb;
+            vdw += (long long)no * VP.ninp[l];
+            vdb += no;
+            if (!head) { vs += (long long)vin * no + no; vin = no; }
+            if (E->vhid[l] > maxw && !head) maxw = E->vhid[l];
+        }
+        if (E->tc_wvb < (size_t)vdw || E->tc_hdv < (size_t)N) {
+            cudaFree(E->Wvb); cudaFree(E->Bvf); cudaFree(E->HDv);
+            E->Wvb = nullptr; E->Bvf = nullptr; E->HDv = nullptr; E->tc_wvb = 0; E->tc_hdv = 0;
+            CKR(cudaMalloc(&E->Wvb, (size_t)vdw * 2), );
+            CKR(cudaMalloc(&E->Bvf, (size_t)vdb * 4), );
+            CKR(cudaMalloc(&E->HDv, (size_t)N * 32 * 4), );
+            E->tc_wvb = vdw; E->tc_hdv = N;
+        }
+    }
     // buffers (allocated on first use, kept by the env)
     if (E->tc_N < (size_t)N || E->tc_w < (size_t)maxw) {
         cudaFree(E->Xb); cudaFree(E->Hb[0]); cudaFree(E->Hb[1]); cudaFree(E->HD);
@@ -1071,6 +1135,10 @@ static void rollout_tc(EnvState* E, int H, const float* W, const float* mean, co
     if (!E->derr) { CKR(cudaMalloc(&E->derr, sizeof(int)), ); CKR(cudaMemset(E->derr, 0, sizeof(int)), ); }
     k_repack_bf16<<<240, 256, 0, E->stream>>>(W, E->Wb, E->Bf, E->LS, RP);
     CKR(cudaGetLastError(), );
+    if (vnet) {
+        k_repack_bf16_value<<<240, 256, 0, E->stream>>>(W, E->Wvb, E->Bvf, VP);
+        CKR(cudaGetLastError(), );
+    }
     Params P = base_params(E);
     P.mode = MODE_ROLLOUT; P.H = 1; P.ext_policy = 1;
     P.mean = mean; P.var = var;
@@ -1094,7 +1162,22 @@ static void rollout_tc(EnvState* E, int H, const float* W, const float* mean, co
         cudaError_t e = dense_tc(N, 32, k, in, k, E->Wb + RP.dstW[nh], E->Bf + RP.dstB[nh], -1, E->HD, 32, nullptr, 0,
                                  E->derr, E->stream);
         if (e != cudaSuccess) { set_error((int)e, "rollout_tc", cudaGetErrorString(e)); return false; }
-        k_sample<<<(N + 127) / 128, 128, 0, E->stream>>>(P, row, E->HD, E->LS, tick);
+        if (vnet) {  // value network on the same normalised observations
+            in = E->Xb;
+            k = XK;
+            for (int l = 0; l < E->vnh; ++l) {
+                __nv_bfloat16* out = E->Hb[l & 1];
+                e = dense_tc(N, E->vhid[l], k, in, k, E->Wvb + VP.dstW[l], E->Bvf + VP.dstB[l], E->act, nullptr, 0, out,
+                             E->vhid[l], E->derr, E->stream);
+                if (e != cudaSuccess) { set_error((int)e, "rollout_tc", cudaGetErrorString(e)); return false; }
+                in = out;
+                k = E->vhid[l];
+            }
+            e = dense_tc(N, 32, k, in, k, E->Wvb + VP.dstW[E->vnh], E->Bvf + VP.dstB[E->vnh], -1, E->HDv, 32, nullptr, 0,
+                         E->derr, E->stream);
+            if (e != cudaSuccess) { set_error((int)e, "rollout_tc", cudaGetErrorString(e)); return false; }
+        }
+        k_sample<<<(N + 127) / 128, 128, 0, E->stream>>>(P, row, E->HD, vnet ? E->HDv : E->HD, E->LS, tick);
         return cudaGetLastError() == cudaSuccess;
     };
     for (int t = 0; t < H; ++t) {
@@ -1202,7 +1285,7 @@ void g1_env_destroy(void* h) {  // g1_env.cu:469-474
     cudaFree(E->dact); cudaFree(E->dobs); cudaFree(E->drew); cudaFree(E->ddone);
     cudaFree(E->WT); cudaFree(E->ncon_hist); cudaFree(E->ncon_last);
     cudaFree(E->Xb); cudaFree(E->Hb[0]); cudaFree(E->Hb[1]); cudaFree(E->Wb); cudaFree(E->Bf); cudaFree(E->LS);
-    cudaFree(E->HD); cudaFree(E->derr); cudaFree(E->tf_img);
+    cudaFree(E->HD); cudaFree(E->derr); cudaFree(E->tf_img); cudaFree(E->Wvb); cudaFree(E->Bvf); cudaFree(E->HDv);
     delete E;
 }
 
@@ -1243,6 +1326,22 @@ int g1_env_set_policy_ex(void* h, int nh, const int* hidden, int activation, int
         }
     E->nh = nh; E->act = activation; E->prec = 1;
     for (int i = 0; i < MAX_HIDDEN; ++i) E->hid[i] = i < nh ? hidden[i] : 0;
+    return 0;
+}
+
+// extension: a separate value network of nh hidden layers (widths
+// multiples of 8 in [8, 1024], the policy's activation) on the tensor-core policy path;
+// nh = 0 returns to the shared trunk's value head.  Returns 0 on success.
+int g1_env_set_value_net(void* h, int nh, const int* hidden) {
+    EnvState* E = (EnvState*)h;
+    if (nh < 0 || nh > MAX_HIDDEN) { set_error(-22, "g1_env_set_value_net", "invalid"); return -22; }
+    for (int i = 0; i < nh; ++i)
+        if (hidden[i] < 8 || hidden[i] > 1024 || (hidden[i] & 7)) {
+            set_error(-22, "g1_env_set_value_net", "widths must be multiples of 8 in [8, 1024]");
+            return -22;
+        }
+    E->vnh = nh;
+    for (int i = 0; i < MAX_HIDDEN; ++i) E->vhid[i] = i < nh ? hidden[i] : 0;
     return 0;
 }
 
@@ -1343,6 +1442,10 @@ void g1_rollout(void* h, int H, const float* W, const float* mean, const float* 
     if (H <= 0) return;
     if (E->prec == 1) {
         rollout_tc(E, H, W, mean, var, O, A, LP, V, R, D, Vlast);
+        return;
+    }
+    if (E->vnh > 0) {
+        set_error(-22, "g1_rollout", "a separate value network needs the tensor-core policy (precision 1)");
         return;
     }
     size_t need = policy_floats(E->nh, E->hid);

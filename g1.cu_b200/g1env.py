@@ -49,6 +49,7 @@ SIGNATURES = {
     "g1_env_set_friction": (None, [_vp, ctypes.c_float]),
     "g1_env_set_policy_ex": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int]),
     "g1_env_tc_status": (ctypes.c_int, [_vp]),
+    "g1_env_set_value_net": (ctypes.c_int, [_vp, ctypes.c_int, _vp]),
     "g1_env_get_state": (None, [_vp, _vp, _vp, _vp, _vp, _vp]),
     "g1_env_set_state": (None, [_vp, _vp, _vp, _vp, _vp, ctypes.c_ulonglong]),
     "g1_env_ncon_hist": (None, [_vp, ctypes.c_int, _vp]),
@@ -153,6 +154,13 @@ class G1Env:
 
     def tc_status(self):
         return _lib.g1_env_tc_status(self.h)
+
+    def set_value_net(self, hidden=()):
+        """Separate value network (BASELINE config 4) for the bf16 tensor-core policy path;
+        () returns to the shared trunk's value head."""
+        hid = np.ascontiguousarray(hidden if len(hidden) else [0], np.int32)
+        if _lib.g1_env_set_value_net(self.h, len(hidden), _dp(hid)):
+            _check()
 
     def set_friction(self, mu):
         _lib.g1_env_set_friction(self.h, float(mu))
@@ -344,32 +352,49 @@ class RunNorm:
 
 # ---------------- actor-critic (ppo.py:85-99) ----------------
 class AC(nn.Module):
-    def __init__(self, obs_dim, act_dim, hidden=(256, 256), activation="tanh"):
+    """The reference's actor-critic (shared trunk, value head on the last hidden layer).
+    value_hidden: a separate value network of those widths instead."""
+
+    def __init__(self, obs_dim, act_dim, hidden=(256, 256), activation="tanh", value_hidden=None):
         super().__init__()
+        act = (lambda: nn.Tanh()) if activation == "tanh" else (lambda: nn.ELU())
         layers, d = [], obs_dim
         for h in hidden:
-            layers += [nn.Linear(d, h), nn.Tanh() if activation == "tanh" else nn.ELU()]
+            layers += [nn.Linear(d, h), act()]
             d = h
         self.hidden = tuple(hidden)
         self.activation = activation
+        self.value_hidden = tuple(value_hidden) if value_hidden else None
         self.body = nn.Sequential(*layers)
         self.mu = nn.Linear(d, act_dim)
-        self.v = nn.Linear(d, 1)
+        if self.value_hidden:
+            vl, dv = [], obs_dim
+            for h in self.value_hidden:
+                vl += [nn.Linear(dv, h), act()]
+                dv = h
+            self.v_body = nn.Sequential(*vl)
+            self.v = nn.Linear(dv, 1)
+        else:
+            self.v = nn.Linear(d, 1)
         self.log_std = nn.Parameter(-0.5 * torch.ones(act_dim))
 
     def forward(self, x):
         z = self.body(x)
-        return self.mu(z), self.log_std.exp(), self.v(z).squeeze(-1)
+        v = self.v(self.v_body(x)) if self.value_hidden else self.v(z)
+        return self.mu(z), self.log_std.exp(), v.squeeze(-1)
 
 
 def pack_weights(ac):
     """Flatten AC params in the order the kernel unpacks (ppo_fused.py:35-44): per hidden
-    layer W,b; then Wmu,bmu, Wv,bv, log_std.  nn.Linear weight is [out,in] row-major."""
-    parts = []
-    for m in ac.body:
-        if isinstance(m, nn.Linear):
-            parts += [m.weight.reshape(-1), m.bias]
-    parts += [ac.mu.weight.reshape(-1), ac.mu.bias, ac.v.weight.reshape(-1), ac.v.bias, ac.log_std]
+    layer W,b; then Wmu,bmu, Wv,bv, log_std.  nn.Linear weight is [out,in] row-major.
+    With a separate value network (g1_env_set_value_net): per policy hidden layer W,b; Wmu,
+    bmu, log_std; per value hidden layer W,b; Wv, bv."""
+    lin = lambda seq: [t for m in seq if isinstance(m, nn.Linear) for t in (m.weight.reshape(-1), m.bias)]
+    parts = lin(ac.body)
+    if getattr(ac, "value_hidden", None):
+        parts += [ac.mu.weight.reshape(-1), ac.mu.bias, ac.log_std] + lin(ac.v_body) + [ac.v.weight.reshape(-1), ac.v.bias]
+    else:
+        parts += [ac.mu.weight.reshape(-1), ac.mu.bias, ac.v.weight.reshape(-1), ac.v.bias, ac.log_std]
     return torch.cat(parts).contiguous()
 
 

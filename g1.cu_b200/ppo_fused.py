@@ -1,8 +1,13 @@
 """PPO on the fused GPU rollout, one process per GPU (the reference's scripts/ppo_fused.py
 training loop, ppo_fused.py:47-171, with world sharding across ranks).
 
-    python g1.cu_b200/ppo_fused.py [iters] [n_worlds_per_gpu] [--smoke] [--tag=name]
+    python g1.cu_b200/ppo_fused.py [iters] [n_worlds_per_gpu] [--smoke] [--tag=name] [--config4] [--no-eval]
     torchrun --nproc-per-node 8 g1.cu_b200/ppo_fused.py 1500 8192
+    torchrun --nproc-per-node 8 g1.cu_b200/ppo_fused.py 3 65536 --config4 --no-eval
+
+--config4: policy 100-1024-1024-512-29 ELU on the bf16 tensor-core path plus a separate
+100-512-512-512-1 value network; each iteration prints its wall time split into rollout and
+update (and the rollout's substeps/s).
 
 The rollout runs in the CUDA library (g1_rollout); torch does only the PPO update, reading
 the trajectory buffers in place.  With WORLD_SIZE > 1 each rank owns its own worlds (global
@@ -126,6 +131,8 @@ def main():
     iters = int(args[0]) if args else (3 if smoke else 1500)
     N = int(args[1]) if len(args) > 1 else (256 if smoke else 8192)
     H = 16 if smoke else 32
+    config4 = "--config4" in sys.argv
+    do_eval = "--no-eval" not in sys.argv
     tag = next((a.split("=", 1)[1] for a in sys.argv if a.startswith("--tag=")), "fused")
     out_dir = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "runs")
     os.makedirs(out_dir, exist_ok=True)
@@ -133,7 +140,12 @@ def main():
     env = G1Env(N, substeps=10, pgs_iters=8, seed=1, device=local, world0=rank * N)
     O_dim, A_dim = env.obs_dim, env.act_dim
     torch.manual_seed(0)
-    ac = AC(O_dim, A_dim).to(dev)
+    if config4:
+        env.set_policy((1024, 1024, 512), "elu", precision="bf16")
+        env.set_value_net((512, 512, 512))
+        ac = AC(O_dim, A_dim, (1024, 1024, 512), "elu", value_hidden=(512, 512, 512)).to(dev)
+    else:
+        ac = AC(O_dim, A_dim).to(dev)
     broadcast_params(ac)
     norm = RunNorm(O_dim, dev)
     opt = torch.optim.Adam(ac.parameters(), lr=3e-4)
@@ -145,16 +157,25 @@ def main():
         logf.write("iter,mean_ep_rew_step,ret,loss,fwd_mean,ep_len,fall_rate,vx_mean,sps\n")
     t0 = time.time()
     for it in range(iters):
+        torch.cuda.synchronize()
+        t_it = time.time()
         fmean, fvar = norm.mean.clone(), norm.var.clone()
         W = pack_weights(ac).detach()
         env.rollout(H, W, fmean, fvar, O, A, LP, V, R, D, Vlast)
+        torch.cuda.synchronize()
+        t_roll = time.time() - t_it
         with torch.no_grad():
             nobs, b_adv, ret = prepare_batch(norm, O, V, R, D, Vlast, fmean, fvar)
         loss = ppo_update(ac, opt, nobs.reshape(-1, O_dim), A.reshape(-1, A_dim), LP.reshape(-1), b_adv.reshape(-1),
                           ret.reshape(-1))
+        torch.cuda.synchronize()
+        t_iter = time.time() - t_it
+        if rank == 0 and config4:
+            print(f"iter {it}: wall {t_iter:.3f} s (rollout {t_roll:.3f} s = {world * N * H * 10 / t_roll:.3e} "
+                  f"substeps/s, batch prep + PPO update {t_iter - t_roll:.3f} s)", flush=True)
         sps = world * (it + 1) * H * N / (time.time() - t0)
         ev = {"fwd_mean": float("nan"), "ep_len_mean": float("nan"), "fall_rate": float("nan"), "vx_mean": float("nan")}
-        if rank == 0 and ((it % 25 == 0) or it == iters - 1):
+        if rank == 0 and do_eval and ((it % 25 == 0) or it == iters - 1):
             ev = evaluate(env, ac, norm, dev, steps=400 if not smoke else 20)
             torch.save(dict(model=ac.state_dict(), obs_mean=norm.mean, obs_var=norm.var),
                        os.path.join(out_dir, f"{tag}_last.pt"))

@@ -105,6 +105,13 @@ int g1_env_set_policy(void* h, int nh, const int* hidden, int activation);
  * in-kernel policy always on FFMA.  Returns 0 on success. */
 int g1_env_set_policy_ex(void* h, int nh, const int* hidden, int activation, int policy_precision);
 
+/* extension: a separate value network of nh hidden layers (widths multiples
+ * of 8 in [8, 1024], the policy's activation), used by g1_rollout with policy_precision 1;
+ * nh = 0 returns to the shared trunk's value head (the reference's AC, ppo.py:85-99).  With a
+ * value network the packed weights are [policy hidden layers W, b][Wmu][bmu][log_std][value
+ * hidden layers W, b][Wv (1 x last)][bv].  Returns 0 on success. */
+int g1_env_set_value_net(void* h, int nh, const int* hidden);
+
 /* extension: nonzero if a tensor-core wait of the bf16 policy path timed out since the last
  * call (synchronous; clears the flag). */
 int g1_env_tc_status(void* h);

@@ -67,3 +67,42 @@ def test_config3_policy_means_and_physics():
     assert np.array_equal(g[3], o[3]) and g[4] == o[4] == H
     env.close()
 
+
+
+def test_config4_separate_value_network():
+    """BASELINE config 4's networks: the config-3 policy plus a separate 100-512-512-512-1 value
+    MLP (g1_env_set_value_net).  Means within 1e-2 of fp32; the value within 1e-2 of a torch
+    reference rounding weights and activations to bf16 where the kernel does."""
+    import g1env
+    N, H, VH = 300, 2, (512, 512, 512)
+    env = g1env.G1Env(N, 10, 8, seed=17)
+    env.set_policy(HID, "elu", precision="bf16")
+    env.set_value_net(VH)
+    env.reset()
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, HID, "elu", value_hidden=VH).cuda(), seed=5)
+    with torch.no_grad():
+        ac.log_std.fill_(-20.0)
+        ac.v.bias.fill_(0.3)
+    W = g1env.pack_weights(ac).detach()
+    mean, var = torch.zeros(100, device="cuda"), torch.ones(100, device="cuda")
+    z = lambda *s: torch.zeros(*s, device="cuda")
+    O, A, LP, V, R, D, Vl = z(H, N, 100), z(H, N, 29), z(H, N), z(H, N), z(H, N), z(H, N), z(N)
+    env.rollout(H, W, mean, var, O, A, LP, V, R, D, Vl)
+    torch.cuda.synchronize()
+    assert env.tc_status() == 0
+    with torch.no_grad():
+        for t in range(H):
+            x = torch.clamp((O[t] - mean) / torch.sqrt(var + 1e-8), -10, 10)
+            mu, _, v = ac(x)
+            assert ((A[t] - mu).norm() / mu.norm()).item() <= 1e-2
+            h = x.to(torch.bfloat16).float()
+            for m in ac.v_body:
+                if isinstance(m, torch.nn.Linear):
+                    h = h @ m.weight.to(torch.bfloat16).float().T + m.bias
+                else:
+                    h = torch.nn.functional.elu(h).to(torch.bfloat16).float()
+            vb = (h @ ac.v.weight.to(torch.bfloat16).float().T + ac.v.bias).squeeze(-1)
+            assert ((V[t] - vb).norm() / vb.norm()).item() <= 1e-2
+            assert ((V[t] - v).norm() / v.norm()).item() <= 5e-2
+    env.set_value_net(())
+    env.close()

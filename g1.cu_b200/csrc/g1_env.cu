@@ -28,6 +28,7 @@
 
 #include "g1_physics.cuh"
 #include "g1_mlp_tc.cuh"
+#include "g1_gemm_tma.cuh"
 #include "../../include/g1env.h"
 
 using namespace g1;
@@ -1055,8 +1056,69 @@ static cudaError_t launch_dense_tc(int M, int N, int K, const __nv_bfloat16* X, 
     g1tc::k_dense_tc<BN><<<grid, g1tc::NTH, smem, stream>>>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err);
     return cudaGetLastError();
 }
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    return fn;
+}
+
+// 2-D bf16 row-major [rows][ld] tensor, box {64 columns, box_rows}, 128-byte swizzle,
+// out-of-range elements read as zero
+static bool make_map(CUtensorMap* m, const void* base, int cols, int rows, int ld, int box_rows) {
+    EncodeTiledFn f = encode_fn();
+    if (!f) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)g1gemm::BK, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+static cudaError_t launch_gemm_tma(int M, int N, int K, const __nv_bfloat16* X, int ldx, const __nv_bfloat16* W,
+                                   const float* bias, int act, float* of, int ldo, __nv_bfloat16* ob, int ldob, int* err,
+                                   cudaStream_t stream) {
+    static int attr_dev = -1;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int smem = g1gemm::smem_bytes<BN>();
+    if (attr_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(g1gemm::k_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr_dev = dev;
+    }
+    CUtensorMap mx, mw;
+    if (!make_map(&mx, X, K, M, ldx, g1gemm::BM) || !make_map(&mw, W, K, N, K, BN)) return cudaErrorInvalidValue;
+    const int tiles = ((M + g1gemm::BM - 1) / g1gemm::BM) * ((N + BN - 1) / BN);
+    const int grid = tiles < nsm ? tiles : nsm;
+    g1gemm::k_gemm<BN><<<grid, g1gemm::NTH, smem, stream>>>(mx, mw, M, N, K, bias, act, ob, of, of ? ldo : ldob, err);
+    return cudaGetLastError();
+}
+
 static cudaError_t dense_tc(int M, int N, int K, const __nv_bfloat16* X, int ldx, const __nv_bfloat16* W, const float* bias,
                             int act, float* of, int ldo, __nv_bfloat16* ob, int ldob, int* err, cudaStream_t stream) {
+    // TMA path: 16-byte aligned operands with 16-byte row pitches
+    const bool tma = (K % 8 == 0) && (ldx % 8 == 0) && ((((uintptr_t)X) | ((uintptr_t)W)) % 16 == 0) && encode_fn();
+    if (tma) {
+        if (N <= 32) return launch_gemm_tma<32>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+        if (N <= 64) return launch_gemm_tma<64>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+        if (N <= 128) return launch_gemm_tma<128>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+        return launch_gemm_tma<256>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
+    }
     if (N <= 32) return launch_dense_tc<32>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
     if (N <= 64) return launch_dense_tc<64>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);
     return launch_dense_tc<256>(M, N, K, X, ldx, W, bias, act, of, ldo, ob, ldob, err, stream);

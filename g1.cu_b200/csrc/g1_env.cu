@@ -553,16 +553,16 @@ struct SmemPlan {
 __host__ __device__ inline SmemPlan smem_plan() {
     SmemPlan p;
     p.tab_floats = ((int)((sizeof(G1Tables) + 15) / 16)) * 4;
-    p.group_floats = GROUP_FLOATS + GW * 36;  // + per-world damping rows (k_qacc)
+    p.group_floats = GROUP_FLOATS;
     p.tf_floats = p.tab_floats + NWARPS * p.group_floats + 4 + MAX_WB;
     p.total_bytes = (p.tf_floats + 16 + 2 * 16) * 4;
     return p;
 }
-static_assert(((((int)((sizeof(G1Tables) + 15) / 16)) * 4 + NWARPS * (GROUP_FLOATS + GW * 36) + 4 + MAX_WB) & 1) == 0,
+static_assert(((((int)((sizeof(G1Tables) + 15) / 16)) * 4 + NWARPS * GROUP_FLOATS + 4 + MAX_WB) & 1) == 0,
               "mbarriers need 8-byte alignment");
 // policy scratch of the tensor-core MLP inside the frames (g1_mlp_tc.cuh: activations,
 // weight stages, head outputs), 128 bytes of alignment slack
-static_assert(128 + g1tc::TF_SCRATCH <= NWARPS * (GROUP_FLOATS + GW * 36) * 4, "tensor-core MLP scratch must fit in the frames");
+static_assert(128 + g1tc::TF_SCRATCH <= NWARPS * GROUP_FLOATS * 4, "tensor-core MLP scratch must fit in the frames");
 static_assert(sizeof(g1tc::TfShared) <= (16 + 2 * 16) * 4, "tensor-core MLP state must fit its smem slot");
 static_assert(MAX_WB * XSTR + 2 * MAX_WB * 260 + KT * OC <= NWARPS * GROUP_FLOATS, "MLP activations must fit in the frames");
 
@@ -699,7 +699,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* grp = smem + plan.tab_floats + warp * plan.group_floats;
     float* cw = grp + GW * WFLOATS;
-    float* bd = cw + CFLOATS;  // [GW][36]
     for (int s0 = (blockIdx.x * NWARPS + warp) * GW; s0 < n; s0 += gridDim.x * NWARPS * GW) {
         const int nvalid = min(GW, n - s0);
         for (int it = lane; it < GW * 36; it += 32) {
@@ -710,7 +709,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, 
             fr[WL::QP + i] = ok && i < NQ ? qpos[st * NQ + i] : (i < NQ ? T.qpos_stand[i] : 0.f);
             fr[WL::QV + i] = ok && i < NV ? qvel[st * NV + i] : 0.f;
             fr[WL::TAU + i] = ok && i < NV && tau ? tau[st * NV + i] : 0.f;
-            bd[w * 36 + i] = ok && i < NV && bdt ? bdt[st * NV + i] : 0.f;
         }
         __syncwarp();
         const float* bdt_w[GW];
@@ -720,7 +718,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, 
 #pragma unroll
         for (int w = 0; w < GW; ++w) {
             const bool ok = w < nvalid;
-            bdt_w[w] = bd + w * 36;
+            bdt_w[w] = (ok && bdt) ? bdt + (size_t)(s0 + w) * NV : nullptr;  // damping rows read from global
             bias_w[w] = (ok && bias_out) ? bias_out + (size_t)(s0 + w) * NV : nullptr;
             f_w[w] = (ok && f_out) ? f_out + (size_t)(s0 + w) * MAXEFC : nullptr;
             qs_w[w] = (ok && qacc_s_out) ? qacc_s_out + (size_t)(s0 + w) * NV : nullptr;

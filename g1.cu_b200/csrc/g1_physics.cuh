@@ -143,10 +143,11 @@ struct WL {  // per-world frame, offsets in floats
         FU6 = 604,            // base U6 [36]
         FL6 = 640,            // base Dm -> Cholesky factor [36]
         XS = 676,             // kept body frames (pelvis, feet): quat [4] + pos [3] (+1) per slot
-        BQ = 708,             // per body: quat [4] + (xipos - p) [3]  (F1 -> B1)
-        FOWN = 928,           // per body: own force, then subtree force [31][6]
-        UB = 1114,            // per body: u_b [31] (+1)
-        HF = 1146,            // F1 branch hand-off: pos, quat, w, v, aw, av [19] (+1) per branch slot
+        BQ = 708,             // per body (F1 -> B1): world rotational inertia, upper triangle
+                              // [xx xy xz yy yz zz], then xipos - p [3]
+        FOWN = BQ + 280,      // per body: own force, then subtree force [31][6]
+        UB = FOWN + 186,      // per body: u_b [31] (+1)
+        HF = UB + 32,         // F1 branch hand-off: pos, quat, w, v, aw, av [19] (+1) per branch slot
         HA = HF + 20 * G1_MAXBRANCH,   // F2 branch hand-off: spatial acceleration [6] (+2)
         HB = HA + 8 * G1_MAXBRANCH,    // B1 chain-head contributions: IA [21], f [6], pA [6] (+3)
         A1 = HB + 36 * 4,     // base spatial acceleration [6] (+2)
@@ -205,22 +206,25 @@ __device__ __forceinline__ float dcoef(int k, int a) {
 }
 
 // ------------------------------------------------------------------ tree sweeps
-// body force of body b from its frame and spatial velocity / acceleration
-__device__ __forceinline__ void body_force_at(const G1Tables& T, int b, Q4 quat, V3 cpos, V3 w, V3 v, V3 aw, V3 av, float* f_out) {
+// body force of body b from its frame and spatial velocity / acceleration, also keeping the
+// upper triangle of its world inertia and its com offset in bi[9] for the leaf -> root sweep
+__device__ __forceinline__ void body_force_keep(const G1Tables& T, int b, Q4 quat, V3 cpos, V3 w, V3 v, V3 aw, V3 av,
+                                                float* f_out, float* bi) {
     float Iw[9];
     V3 c;
     world_inertia(T, b, quat, cpos, mk3(0, 0, 0), Iw, c);
+    bi[0] = Iw[0]; bi[1] = Iw[1]; bi[2] = Iw[2]; bi[3] = Iw[4]; bi[4] = Iw[5]; bi[5] = Iw[8];
+    st3(bi + 6, c);
     V3 fw, fv;
     body_force(Iw, c, T.body_mass[b], w, v, aw, av, fw, fv);
     st3(f_out, fw);
     st3(f_out + 3, fv);
 }
-// spatial inertia (packed 21) of body b from its orientation and com offset from the pelvis
-__device__ __forceinline__ void body_ia_at(const G1Tables& T, int b, Q4 quat, V3 cpos, float* ia) {
-    float Iw[9];
-    V3 c;
-    world_inertia(T, b, quat, cpos, mk3(0, 0, 0), Iw, c);
-    spatial_inertia21(Iw, c, T.body_mass[b], ia);
+// spatial inertia (packed 21) of body b from the kept world inertia (upper triangle -- the
+// only entries spatial_inertia21 reads) and com offset
+__device__ __forceinline__ void body_ia_kept(const G1Tables& T, int b, const float* bi, float* ia) {
+    const float Iw[9] = {bi[0], bi[1], bi[2], bi[1], bi[3], bi[4], bi[2], bi[4], bi[5]};
+    spatial_inertia21(Iw, ld3(bi + 6), T.body_mass[b], ia);
 }
 
 // The smooth part of the per-substep dynamics for the GW worlds of a warp (qp, qv, tau in each
@@ -302,8 +306,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
             float* xs = XS + 8 * T.xslot[1];
             st4(xs, q1); st3(xs + 4, p);
             const V3 cpos = sub3(add3(p, qrot(q1, ld3(T.body_ipos + 3))), p);  // xipos - p, as the reference rounds it
-            st4(BQ + 7, q1); st3(BQ + 11, cpos);
-            body_force_at(T, 1, q1, cpos, bw, bv, baw, bav, FOWN + 6);
+            body_force_keep(T, 1, q1, cpos, bw, bv, baw, bav, FOWN + 6, BQ + 9);
         }
     }
 
@@ -338,7 +341,6 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                     st4(xs, quat); st3(xs + 4, pos);
                 }
                 const V3 cpos = sub3(add3(pos, qrot(quat, ld3(T.body_ipos + 3 * b))), p);
-                st4(BQ + 7 * b, quat); st3(BQ + 7 * b + 4, cpos);
                 const V3 sw = qrot(quat, ax);
                 const V3 sv = cross3(sub3(add3(pos, qrot(quat, an)), p), sw);
                 st3(S + 6 * d, sw); st3(S + 6 * d + 3, sv);
@@ -348,7 +350,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                 vv = {vv.x + sv.x * qd, vv.y + sv.y * qd, vv.z + sv.z * qd};
                 aw = {aw.x + sdw.x * qd, aw.y + sdw.y * qd, aw.z + sdw.z * qd};
                 av = {av.x + sdv.x * qd, av.y + sdv.y * qd, av.z + sdv.z * qd};
-                body_force_at(T, b, quat, cpos, wv, vv, aw, av, FOWN + 6 * b);
+                body_force_keep(T, b, quat, cpos, wv, vv, aw, av, FOWN + 6 * b, BQ + 9 * b);
                 if (T.branch_slot[b] >= 0) {
                     float* st = fr + WL::HF + 20 * T.branch_slot[b];
                     st3(st, pos); st4(st + 3, quat); st3(st + 7, wv); st3(st + 10, vv); st3(st + 13, aw); st3(st + 16, av);
@@ -371,7 +373,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
             if (k >= 0 && k < len) {
                 const int b = T.chain_body[cl][len - 1 - k], d = T.dofadr[b];
                 float ia[21], f[6], pa[6];
-                body_ia_at(T, b, ld4(BQ + 7 * b), ld3(BQ + 7 * b + 4), ia);
+                body_ia_kept(T, b, BQ + 9 * b, ia);
 #pragma unroll
                 for (int i = 0; i < 6; ++i) { f[i] = FOWN[6 * b + i]; pa[i] = 0.f; }
                 for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
@@ -444,7 +446,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
     float base_ia[21], base_f[6], base_pa[6];
     if (w < GW) {
         // every lane of the world pulls the pelvis children (descending) into registers
-        body_ia_at(T, 1, ld4(BQ + 7), ld3(BQ + 11), base_ia);
+        body_ia_kept(T, 1, BQ + 9, base_ia);
 #pragma unroll
         for (int i = 0; i < 6; ++i) { base_f[i] = FOWN[6 + i]; base_pa[i] = 0.f; }
         for (int q = T.child_start[1]; q < T.child_start[2]; ++q) {

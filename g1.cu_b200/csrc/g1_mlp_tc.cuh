@@ -263,6 +263,7 @@ constexpr int TF_STAGE = 3 * 4096 * 2;           // 24 KB: one chunk of N x kc w
 constexpr int TF_NSTAGE = 4;
 constexpr int TF_HDBYTES = TF_ROWS * 32 * 4;     // head outputs, fp32 [64][32]
 constexpr int TF_SCRATCH = TF_ABYTES + TF_NSTAGE * TF_STAGE + TF_HDBYTES;
+static_assert(TF_ROWS * (TF_KMAX + 4) * 4 <= TF_NSTAGE * TF_STAGE, "hidden-layer epilogue staging must fit in the stages");
 constexpr int TF_MMA_WARP = 2, TF_COPY_WARP = 3;  // lane 0 of each; idle in the epilogue (rows < 64)
 
 // K width of one weight chunk of an N-wide layer: the largest multiple of 16 with N kc <= 4096
@@ -437,7 +438,9 @@ __device__ void tf_layer(TfShared* S, uint8_t* A, uint8_t* stages, const TfLayer
                      : "memory");
     } else if (warp == TF_COPY_WARP && lane == 0) {
         for (int c = (int)S->st[5]; c < nchunk; ++c) ok &= tf_issue(S, stages, L, c, g0 + c);
-        if (nxt) ok &= tf_prefetch(S, stages, *nxt, g0 + nchunk);
+        // a hidden layer's epilogue stages its sums in the weight stages: the next layer's
+        // chunks are queued by that layer itself
+        if (nxt && act < 0) ok &= tf_prefetch(S, stages, *nxt, g0 + nchunk);
         else S->st[5] = 0;
     }
     // every thread: wait for the layer's MMAs
@@ -447,9 +450,15 @@ __device__ void tf_layer(TfShared* S, uint8_t* A, uint8_t* stages, const TfLayer
 #ifdef G1_PROF
     PROF_MARK(P_TF_MMA);
 #endif
-    // epilogue: TMEM lane r = row r; warps w and w+4 share lanes 32(w&3).. and split the columns
+    // epilogue.  TMEM lane r = row r: only warps w with 32 (w & 3) < rows can read it, and
+    // they sit on two of the SM's four sub-partitions.  Phase 1: those warps (w and w + 4
+    // split the columns) move accumulator sums + bias to fp32 rows in the weight stages
+    // (hidden layers) or straight to hd (the head).  Phase 2 (hidden layers): every warp
+    // applies the activation and writes the three bf16 parts of the next layer's input.
     const int q = warp & 3;
     const int nshare = (q + 4 < NT / 32) ? 2 : 1;
+    float* stg = reinterpret_cast<float*>(stages);
+    const int sld = N + 4;
     if (32 * q < nrows) {
         const int half = N / nshare, c_beg = (warp >> 2) * half, row = 32 * q + lane;
         for (int c0 = c_beg; c0 < c_beg + half; c0 += 8) {
@@ -466,20 +475,33 @@ __device__ void tf_layer(TfShared* S, uint8_t* A, uint8_t* stages, const TfLayer
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             float v[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float x = (__uint_as_float(r[j]) + __uint_as_float(u[j])) + L.bias[c0 + j];
-                if (act == 0) x = tanhf(x);
-                else if (act == 1) x = x > 0.f ? x : expm1f(x);
-                v[j] = x;
-            }
+            for (int j = 0; j < 8; ++j) v[j] = (__uint_as_float(r[j]) + __uint_as_float(u[j])) + L.bias[c0 + j];
             if (row < nrows) {
                 if (act < 0) {
 #pragma unroll
                     for (int j = 0; j < 8; ++j) hd[row * 32 + c0 + j] = v[j];
                 } else {
-                    tf_store8(A, row, c0, v);
+                    float4* dst = reinterpret_cast<float4*>(stg + row * sld + c0);
+                    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+                    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
                 }
             }
+        }
+    }
+    if (act >= 0) {
+        __syncthreads();
+        const int ng = N / 8;
+        for (int e = tid; e < nrows * ng; e += NT) {
+            const int row = e / ng, c0 = (e % ng) * 8;
+            const float4* src = reinterpret_cast<const float4*>(stg + row * sld + c0);
+            const float4 a = src[0], b = src[1];
+            float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (act == 0) v[j] = tanhf(v[j]);
+                else if (act == 1) v[j] = v[j] > 0.f ? v[j] : expm1f(v[j]);
+            }
+            tf_store8(A, row, c0, v);
         }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -1031,15 +1031,21 @@ __device__ void group_integrate(float* grp, const G1Tables& T, int lane, bool gu
         fr[WL::QV + d] = v;
     }
     __syncwarp();
+    // hinge joints in one uniform pass; the free joint of each world (the heavier quaternion
+    // update) on lanes 0..GW-1 in a second pass
     for (int it = lane; it < GW * NJ; it += 32) {
         const int w = it / NJ, j = it % NJ;
+        if (T.jnt_type[j] != 3) continue;
+        float* fr = grp + w * WFLOATS;
+        fr[WL::QP + T.jnt_qposadr[j]] += dt * fr[WL::QV + T.jnt_dofadr[j]];
+    }
+    if (lane < GW) {
+        const int w = lane, j = T.free_jnt;
         float* fr = grp + w * WFLOATS;
         float *qp = fr + WL::QP;
         const float* qv = fr + WL::QV;
         const int qa = T.jnt_qposadr[j], da = T.jnt_dofadr[j];
-        if (T.jnt_type[j] == 3) {
-            qp[qa] += dt * qv[da];
-        } else {
+        {
             qp[qa] += dt * qv[da]; qp[qa + 1] += dt * qv[da + 1]; qp[qa + 2] += dt * qv[da + 2];
             const V3 v = {qv[da + 3] * dt, qv[da + 4] * dt, qv[da + 5] * dt};
             const float ang = sqrtf(v.x * v.x + v.y * v.y + v.z * v.z);

@@ -57,6 +57,7 @@ struct alignas(16) G1Tables {
     int foot_ndof[G1_NFOOT_];
     unsigned char foot_dofs[G1_NFOOT_][G1_CDS];
     int foot_chains[G1_NFOOT_];  // bit c: chain c holds an ancestor of the sphere's body
+    int free_jnt;                // the floating base's free joint (the only non-hinge joint)
     // chain decomposition of the hinge bodies (root->leaf order inside a chain); lane l of
     // a warp walks chain l.  A chain starts at a child of the floating base or of a branch
     // body; f1_start is the sweep step of its head (its parent is done by then).
@@ -233,5 +234,8 @@ static inline void g1_build_tables(G1Tables* T) {
                     if (T->chain_body[c][q] == b) mask |= 1 << c;
         T->foot_chains[s] = mask;
     }
+    T->free_jnt = 0;
+    for (int j = G1_NJ - 1; j >= 0; --j)
+        if (G1M_JNT_TYPE[j] == 0) T->free_jnt = j;
 }
 #endif

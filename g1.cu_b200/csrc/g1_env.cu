@@ -109,7 +109,7 @@ struct Params {
     const float* act_in;
     float *obs_out, *rew_out, *done_out;
     int* ncon_hist;  // [MAXCON+1] contact-count histogram (substeps), may be null
-    int lockstep;    // warps of a CTA walk their worlds in lockstep (named barrier per substep)
+    int lockstep;    // > 0: the CTA's warps meet at a named barrier every `lockstep` substeps
     int* ncon_last;  // [N] contact count of each world's last substep (load balancing)
     int t0;          // trajectory row of the first control step of this launch
     int ext_policy;  // actions already in A[t0..]: skip the in-kernel policy phase
@@ -390,6 +390,11 @@ __device__ __forceinline__ void policy_sample(const Params& P, const float* HD, 
 // ------------------------------------------------------------------ physics phase
 // Named barrier that keeps the CTA's warps on the same substep (so they fetch the same code).
 __device__ __forceinline__ void substep_barrier() { asm volatile("bar.sync 1, %0;" ::"r"(NTHREADS) : "memory"); }
+// The one place the substep barrier is taken: every warp of the CTA -- with or without a group
+// of worlds this round -- calls this for each substep s, so all warps reach the same barriers.
+__device__ __forceinline__ void lockstep_barrier(const Params& P, int s) {
+    if (P.lockstep > 0 && s % P.lockstep == 0) substep_barrier();
+}
 
 // One control step of GW worlds (global ids wid[0 .. nvalid-1]; the remaining slots carry a
 // stand pose and are not written back) by one warp: PD targets, S substeps, reward, done,
@@ -452,7 +457,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
     pd_torque();
     for (int s = 0; s < P.S; ++s) {
         PROF_BEGIN();
-        if (P.lockstep) substep_barrier();
+        lockstep_barrier(P, s);
 #ifdef G1_PROF
         (void)*(volatile const float*)grp;  // bar.sync blocks lazily: make the wait land here
 #endif
@@ -639,7 +644,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
             }
             if (nvalid == 0) {
                 if (P.lockstep)
-                    for (int s = 0; s < P.S; ++s) substep_barrier();
+                    for (int s = 0; s < P.S; ++s) lockstep_barrier(P, s);
                 continue;
             }
             const float* acts = P.mode == MODE_ROLLOUT ? P.A + (size_t)trow * P.N * ACT_DIM

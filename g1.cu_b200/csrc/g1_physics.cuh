@@ -906,7 +906,10 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     // this lane's column of its world's block, in registers (off the row-to-row chain)
     float acol[4 * MAXCON];
 #pragma unroll
-    for (int i = 0; i < 4 * MAXCON; ++i) acol[i] = i < nrow ? AP[apidx(r0 + i, lane)] : 0.f;
+    for (int i = 0; i < 4 * MAXCON; ++i) {
+        if (i >= maxrow) break;  // rows past the batch's largest world are never read
+        acol[i] = i < nrow ? AP[apidx(r0 + i, lane)] : 0.f;
+    }
     for (int itr = 0; itr < opt.pgs_iters; ++itr) {
 #pragma unroll
         for (int i = 0; i < 4 * MAXCON; ++i) {

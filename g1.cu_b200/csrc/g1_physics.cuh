@@ -170,6 +170,7 @@ struct CL {  // per-warp contact workspace, offsets in floats
     };
 };
 constexpr int WFLOATS = (WL::SIZE + 3) & ~3;
+static_assert(WL::S % 2 == 0 && WL::FU % 2 == 0, "U and S rows are read as float2 (frames are 16-byte aligned)");
 constexpr int CFLOATS = (CL::SIZE + 3) & ~3;
 constexpr int GROUP_FLOATS = GW * WFLOATS + CFLOATS;
 constexpr int MSTR = 35;
@@ -543,22 +544,28 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
         for (int s = 0; s < T.nsteps; ++s) {
             const int k = on ? s - T.chain_start[cl] : -1;
             if (k >= 0 && k < T.chain_len[cl]) {
-                const int b = T.chain_body[cl][k], d = T.dofadr[b];
+                const int b = T.chain_body[cl][k];
+                const int4 bi = T.binfo[b];
+                const int d = bi.x;
                 if (k == 0) {
-                    const int par = T.parent[b];
-                    const float* src = par == 1 ? fr + WL::A1 : fr + WL::HA + 8 * T.branch_slot[par];
+                    const int par = bi.z;
+                    const float* src = par == 1 ? fr + WL::A1 : fr + WL::HA + 8 * T.binfo[par].y;
 #pragma unroll
                     for (int i = 0; i < 6; ++i) a[i] = src[i];
                 }
+                const float2* U2 = reinterpret_cast<const float2*>(FU + 6 * b);
+                const float2 u01 = U2[0], u23 = U2[1], u45 = U2[2];
                 float s2 = 0.f;
-#pragma unroll
-                for (int i = 0; i < 6; ++i) s2 += FU[6 * b + i] * a[i];
+                s2 += u01.x * a[0]; s2 += u01.y * a[1]; s2 += u23.x * a[2];
+                s2 += u23.y * a[3]; s2 += u45.x * a[4]; s2 += u45.y * a[5];
                 const float qdd = (UB[b] - s2) * FINVD[b];
                 qacc[d] = qdd;
-#pragma unroll
-                for (int i = 0; i < 6; ++i) a[i] = a[i] + S[6 * d + i] * qdd;
-                if (T.branch_slot[b] >= 0) {
-                    float* st = fr + WL::HA + 8 * T.branch_slot[b];
+                const float2* S2 = reinterpret_cast<const float2*>(S + 6 * d);
+                const float2 s01 = S2[0], s23 = S2[1], s45 = S2[2];
+                a[0] = a[0] + s01.x * qdd; a[1] = a[1] + s01.y * qdd; a[2] = a[2] + s23.x * qdd;
+                a[3] = a[3] + s23.y * qdd; a[4] = a[4] + s45.x * qdd; a[5] = a[5] + s45.y * qdd;
+                if (bi.y >= 0) {
+                    float* st = fr + WL::HA + 8 * bi.y;
 #pragma unroll
                     for (int i = 0; i < 6; ++i) st[i] = a[i];
                 }
@@ -595,9 +602,10 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
         int b = T.chain_body[c][len - 1], prev = -1;
         for (int k = len - 1; k >= 0; --k) {
             const int bn = k > 0 ? T.chain_body[c][k - 1] : 0;
-            const int d = T.dofadr[b];
+            const int4 bi = T.binfo[b];
+            const int d = bi.x;
             float acc[6];
-            if (T.branch_slot[b] >= 0) {  // branch body: children in descending index
+            if (bi.y >= 0) {  // branch body: children in descending index
 #pragma unroll
                 for (int i = 0; i < 6; ++i) acc[i] = 0.f;
                 for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
@@ -615,14 +623,16 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
 #pragma unroll
                 for (int i = 0; i < 6; ++i) acc[i] = pa[i];
             }
-            const float* sd = S + 6 * d;
-            const float sp = ((((0.f + sd[0] * acc[0]) + sd[1] * acc[1]) + sd[2] * acc[2]) + sd[3] * acc[3]) + sd[4] * acc[4] + sd[5] * acc[5];
+            const float2* S2 = reinterpret_cast<const float2*>(S + 6 * d);
+            const float2 s01 = S2[0], s23 = S2[1], s45 = S2[2];
+            const float sp = ((((0.f + s01.x * acc[0]) + s01.y * acc[1]) + s23.x * acc[2]) + s23.y * acc[3]) + s45.x * acc[4] + s45.y * acc[5];
             const float u = xy[d] - sp;
             xy[d] = u;
             const float ud = u * FINVD[b];
-            const float* U = FU + 6 * b;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) pa[i] = acc[i] + U[i] * ud;
+            const float2* U2 = reinterpret_cast<const float2*>(FU + 6 * b);
+            const float2 u01 = U2[0], u23 = U2[1], u45 = U2[2];
+            pa[0] = acc[0] + u01.x * ud; pa[1] = acc[1] + u01.y * ud; pa[2] = acc[2] + u23.x * ud;
+            pa[3] = acc[3] + u23.y * ud; pa[4] = acc[4] + u45.x * ud; pa[5] = acc[5] + u45.y * ud;
             prev = b;
             b = bn;
         }
@@ -670,32 +680,36 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
     }
 #pragma unroll
     for (int k = 0; k < 6; ++k) xy[k] = q6[k];
-    // root -> leaf, chains first-to-last
+    // root -> leaf, chains first-to-last (U and S rows read as float2: 6-float rows of an
+    // 8-byte aligned frame; the body's dof, branch slot and parent in one 16-byte load)
     for (int c = 0; c < T.nchain; ++c) {
         const int len = T.chain_len[c];
         int b = T.chain_body[c][0];
-        const int par = T.parent[b];
+        const int par = T.binfo[b].z;
         float a[6];
         if (par == 1) {
 #pragma unroll
             for (int i = 0; i < 6; ++i) a[i] = a1[i];
         } else {
-            const float* src = fwd + 6 * T.branch_slot[par];
+            const float* src = fwd + 6 * T.binfo[par].y;
 #pragma unroll
             for (int i = 0; i < 6; ++i) a[i] = src[i];
         }
         for (int k = 0; k < len; ++k) {
             const int bn = k + 1 < len ? T.chain_body[c][k + 1] : 0;
-            const int d = T.dofadr[b];
-            const float* U = FU + 6 * b;
-            const float s2 = ((((0.f + U[0] * a[0]) + U[1] * a[1]) + U[2] * a[2]) + U[3] * a[3]) + U[4] * a[4] + U[5] * a[5];
+            const int4 bi = T.binfo[b];
+            const int d = bi.x;
+            const float2* U2 = reinterpret_cast<const float2*>(FU + 6 * b);
+            const float2 u01 = U2[0], u23 = U2[1], u45 = U2[2];
+            const float s2 = ((((0.f + u01.x * a[0]) + u01.y * a[1]) + u23.x * a[2]) + u23.y * a[3]) + u45.x * a[4] + u45.y * a[5];
             const float qdd = (xy[d] - s2) * FINVD[b];
             xy[d] = qdd;
-            const float* sd = S + 6 * d;
-#pragma unroll
-            for (int i = 0; i < 6; ++i) a[i] = a[i] + sd[i] * qdd;
-            if (T.branch_slot[b] >= 0) {
-                float* dst = fwd + 6 * T.branch_slot[b];
+            const float2* S2 = reinterpret_cast<const float2*>(S + 6 * d);
+            const float2 s01 = S2[0], s23 = S2[1], s45 = S2[2];
+            a[0] = a[0] + s01.x * qdd; a[1] = a[1] + s01.y * qdd; a[2] = a[2] + s23.x * qdd;
+            a[3] = a[3] + s23.y * qdd; a[4] = a[4] + s45.x * qdd; a[5] = a[5] + s45.y * qdd;
+            if (bi.y >= 0) {
+                float* dst = fwd + 6 * bi.y;
 #pragma unroll
                 for (int i = 0; i < 6; ++i) dst[i] = a[i];
             }

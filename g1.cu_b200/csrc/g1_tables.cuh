@@ -58,6 +58,7 @@ struct alignas(16) G1Tables {
     unsigned char foot_dofs[G1_NFOOT_][G1_CDS];
     int foot_chains[G1_NFOOT_];  // bit c: chain c holds an ancestor of the sphere's body
     int free_jnt;                // the floating base's free joint (the only non-hinge joint)
+    int4 binfo[G1_NB];           // per body {dofadr, branch_slot, parent, 0}: one 16-byte load
     // chain decomposition of the hinge bodies (root->leaf order inside a chain); lane l of
     // a warp walks chain l.  A chain starts at a child of the floating base or of a branch
     // body; f1_start is the sweep step of its head (its parent is done by then).
@@ -234,6 +235,7 @@ static inline void g1_build_tables(G1Tables* T) {
                     if (T->chain_body[c][q] == b) mask |= 1 << c;
         T->foot_chains[s] = mask;
     }
+    for (int b = 0; b < G1_NB; ++b) T->binfo[b] = make_int4(T->dofadr[b], T->branch_slot[b], T->parent[b], 0);
     T->free_jnt = 0;
     for (int j = G1_NJ - 1; j >= 0; --j)
         if (G1M_JNT_TYPE[j] == 0) T->free_jnt = j;

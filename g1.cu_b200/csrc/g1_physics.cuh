@@ -35,6 +35,11 @@ __device__ __forceinline__ float dot3(V3 a, V3 b) { return a.x * b.x + a.y * b.y
 __device__ __forceinline__ V3 ld3(const float* p) { return {p[0], p[1], p[2]}; }
 __device__ __forceinline__ void st3(float* p, V3 v) { p[0] = v.x; p[1] = v.y; p[2] = v.z; }
 __device__ __forceinline__ Q4 ld4(const float* p) { return {p[0], p[1], p[2], p[3]}; }
+// six floats [a; b] at an 8-byte aligned address, as three float2 stores
+__device__ __forceinline__ void st6(float* p, V3 a, V3 b) {
+    float2* q = reinterpret_cast<float2*>(p);
+    q[0] = make_float2(a.x, a.y); q[1] = make_float2(a.z, b.x); q[2] = make_float2(b.y, b.z);
+}
 __device__ __forceinline__ void st4(float* p, Q4 q) { p[0] = q.w; p[1] = q.x; p[2] = q.y; p[3] = q.z; }
 // Hamilton product (dynamics.cuh:17-24)
 __device__ __forceinline__ Q4 qmul(Q4 a, Q4 b) {
@@ -170,7 +175,8 @@ struct CL {  // per-warp contact workspace, offsets in floats
     };
 };
 constexpr int WFLOATS = (WL::SIZE + 3) & ~3;
-static_assert(WL::S % 2 == 0 && WL::FU % 2 == 0, "U and S rows are read as float2 (frames are 16-byte aligned)");
+static_assert(WL::S % 2 == 0 && WL::FU % 2 == 0 && WL::FOWN % 2 == 0,
+              "S, U and force rows are accessed as float2 (frames are 16-byte aligned)");
 constexpr int CFLOATS = (CL::SIZE + 3) & ~3;
 constexpr int GROUP_FLOATS = GW * WFLOATS + CFLOATS;
 constexpr int MSTR = 35;
@@ -218,8 +224,7 @@ __device__ __forceinline__ void body_force_keep(const G1Tables& T, int b, Q4 qua
     st3(bi + 6, c);
     V3 fw, fv;
     body_force(Iw, c, T.body_mass[b], w, v, aw, av, fw, fv);
-    st3(f_out, fw);
-    st3(f_out + 3, fv);
+    st6(f_out, fw, fv);
 }
 // spatial inertia (packed 21) of body b from the kept world inertia (upper triangle -- the
 // only entries spatial_inertia21 reads) and com offset
@@ -344,7 +349,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                 const V3 cpos = sub3(add3(pos, qrot(quat, ld3(T.body_ipos + 3 * b))), p);
                 const V3 sw = qrot(quat, ax);
                 const V3 sv = cross3(sub3(add3(pos, qrot(quat, an)), p), sw);
-                st3(S + 6 * d, sw); st3(S + 6 * d + 3, sv);
+                st6(S + 6 * d, sw, sv);
                 const float qd = qv[d];
                 const V3 sdw = cross3(wv, sw), sdv = add3(cross3(wv, sv), cross3(vv, sw));
                 wv = {wv.x + sw.x * qd, wv.y + sw.y * qd, wv.z + sw.z * qd};
@@ -375,8 +380,13 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                 const int b = T.chain_body[cl][len - 1 - k], d = T.dofadr[b];
                 float ia[21], f[6], pa[6];
                 body_ia_kept(T, b, BQ + 9 * b, ia);
+                {
+                    const float2* f2 = reinterpret_cast<const float2*>(FOWN + 6 * b);
+                    const float2 f01 = f2[0], f23 = f2[1], f45 = f2[2];
+                    f[0] = f01.x; f[1] = f01.y; f[2] = f23.x; f[3] = f23.y; f[4] = f45.x; f[5] = f45.y;
+                }
 #pragma unroll
-                for (int i = 0; i < 6; ++i) { f[i] = FOWN[6 * b + i]; pa[i] = 0.f; }
+                for (int i = 0; i < 6; ++i) pa[i] = 0.f;
                 for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
                     const int c = T.child_list[q];
                     if (c == carried) {
@@ -393,8 +403,11 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                     }
                 }
                 float sd[6];
-#pragma unroll
-                for (int i = 0; i < 6; ++i) sd[i] = S[6 * d + i];
+                {
+                    const float2* s2 = reinterpret_cast<const float2*>(S + 6 * d);
+                    const float2 s01 = s2[0], s23 = s2[1], s45 = s2[2];
+                    sd[0] = s01.x; sd[1] = s01.y; sd[2] = s23.x; sd[3] = s23.y; sd[4] = s45.x; sd[5] = s45.y;
+                }
                 const float bd = sd[0] * f[0] + sd[1] * f[1] + sd[2] * f[2] + sd[3] * f[3] + sd[4] * f[4] + sd[5] * f[5];
                 if (bias) bias[d] = bd;
                 const float rhs = -bd + tau[d];
@@ -417,8 +430,10 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                 for (int i = 0; i < 6; ++i) sp += sd[i] * pa[i];
                 const float u = rhs - sp;
                 const float ud = u * invD;
-#pragma unroll
-                for (int i = 0; i < 6; ++i) FU[6 * b + i] = U[i];
+                {
+                    float2* u2 = reinterpret_cast<float2*>(FU + 6 * b);
+                    u2[0] = make_float2(U[0], U[1]); u2[1] = make_float2(U[2], U[3]); u2[2] = make_float2(U[4], U[5]);
+                }
                 FINVD[b] = invD;
                 UB[b] = u;
 #pragma unroll

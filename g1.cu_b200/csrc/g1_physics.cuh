@@ -203,7 +203,7 @@ __device__ unsigned long long g_prof[64];
 #define PROF_RESTART()
 #define PROF_MARK(i) do { } while (0)
 #endif
-enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_CS_LOAD, P_CS_REWARD, P_CS_STORE, P_SORT, P_TOTAL, P_NPHASE };
+enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_CS_LOAD, P_CS_REWARD, P_CS_STORE, P_SORT, P_TOTAL, P_LS_BACK, P_LS_BASE, P_LS_FWD, P_NPHASE };
 
 // pyramid coefficients d_k = DC[k] of the 3-basis (env_qacc.cuh:98-100,154-155)
 __device__ __forceinline__ float dcoef(int k, int a) {
@@ -599,10 +599,24 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
 // its contribution in hand[chain]; a body adds its children in descending child index.
 // u_b = x_d - S_d.pA_b parks in xy[d] between the sweeps; root->leaf a branch body leaves
 // its acceleration in fwd[slot].  `scratch`: SOLVE_SCRATCH floats of this lane.
-__device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, float* xy, float* scratch, int chains) {
-    const float *S = fr + WL::S, *FU = fr + WL::FU, *FINVD = fr + WL::FINVD, *L6 = fr + WL::FL6;
-    float* hand = scratch;
-    float* fwd = scratch + 6 * 4;
+// The factor (frame), the right-hand side (contact workspace row) and the scratch are
+// disjoint shared-memory arrays: the restrict qualifiers let the compiler move a body's loads
+// ahead of the previous body's stores.
+__device__ __noinline__ void lane_solve(const float* __restrict__ fr, const G1Tables& T, float* __restrict__ xy,
+                                       float* __restrict__ scratch, int chains) {
+    const float* __restrict__ S = fr + WL::S;
+    const float* __restrict__ FU = fr + WL::FU;
+    const float* __restrict__ FINVD = fr + WL::FINVD;
+    const float* __restrict__ L6 = fr + WL::FL6;
+    float* __restrict__ hand = scratch;
+    float* __restrict__ fwd = scratch + 6 * 4;
+#ifdef G1_PROF
+    long long _pt = clock64();
+    const bool _lead = (threadIdx.x & 31) == (__ffs(__activemask()) - 1);
+#define LS_MARK(i) do { long long _n = clock64(); if (_lead) atomicAdd(&g_prof[i], (unsigned long long)(_n - _pt)); _pt = _n; } while (0)
+#else
+#define LS_MARK(i) do { } while (0)
+#endif
     // leaf -> root, chains last-to-first; the next body's index is fetched one body ahead.
     // Chains outside `chains` have a zero right-hand side: their pass would produce exact
     // zeros, so it is skipped (their hand-off is zero).
@@ -654,6 +668,7 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
 #pragma unroll
         for (int i = 0; i < 6; ++i) hand[6 * c + i] = pa[i];
     }
+    LS_MARK(P_LS_BACK);
     float pa1[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int q = T.child_start[1]; q < T.child_start[2]; ++q) {
         const float* src = hand + 6 * T.head_chain[T.child_list[q]];
@@ -695,6 +710,7 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
     }
 #pragma unroll
     for (int k = 0; k < 6; ++k) xy[k] = q6[k];
+    LS_MARK(P_LS_BASE);
     // root -> leaf, chains first-to-last (U and S rows read as float2: 6-float rows of an
     // 8-byte aligned frame; the body's dof, branch slot and parent in one 16-byte load)
     for (int c = 0; c < T.nchain; ++c) {
@@ -731,6 +747,8 @@ __device__ __noinline__ void lane_solve(const float* fr, const G1Tables& T, floa
             b = bn;
         }
     }
+    LS_MARK(P_LS_FWD);
+#undef LS_MARK
 }
 
 // ------------------------------------------------------------------ contact

@@ -69,6 +69,7 @@ def test_qacc_vs_reference_cuda_fp32(gpu_qacc, states):
     vp = lambda t: ctypes.c_void_p(t.data_ptr())
     assert L.ref_cuda_qacc(n, *[vp(t) for t in dq], 8, vp(out)) == 0
     e = relrows(gpu_qacc["qacc"], out.cpu().numpy())
+    print(f"qacc vs reference CUDA fp32 over {n} states: max {e.max():.2e}, p99 {np.percentile(e, 99):.2e}")
     assert e.max() <= 1e-5, e.max()
     assert np.percentile(e, 99) <= 5e-6
 
@@ -81,6 +82,8 @@ def test_qacc_vs_fp64_and_fp32_oracle(gpu_qacc, oracle_qacc):
     cond = relrows(o32["qacc"], o64["qacc"])               # fp32 conditioning per state
     e64 = relrows(gpu_qacc["qacc"], o64["qacc"])
     assert np.percentile(e64, 99) <= 1e-5
+    print(f"qacc vs fp64 oracle: p99 {np.percentile(e64, 99):.2e}, max {e64.max():.2e} "
+          f"(reference fp32 vs fp64: max {cond.max():.2e})")
     assert (e64 <= 3 * cond + 1e-5).all(), (e64 - 3 * cond).max()
     assert relrows(gpu_qacc["bias"], o64["bias"]).max() <= 1e-5
     assert relrows(gpu_qacc["qacc_smooth"], o64["qacc_s"]).max() <= 1e-4

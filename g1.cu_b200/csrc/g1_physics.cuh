@@ -770,31 +770,35 @@ struct QaccOpts {
     const float* const* bdt;  // per world slot: shared-memory dt*B diagonal (entries may be null)
 };
 
-// Foot-sphere contacts of the GW worlds (contact.cuh:31-46), lane = 8 w + sphere, compacted
-// in sphere order into each world's CON; returns nothing, ncon in MISC[0].
+// Foot-sphere contacts of the GW worlds (contact.cuh:31-46), lane = 8 (w - w0) + sphere in
+// passes of 32 / 8 worlds, compacted in sphere order into each world's CON; ncon in MISC[0].
 __device__ void group_detect(float* grp, const G1Tables& T, int lane) {
-    static_assert(GW * G1_NFOOT_ <= 32, "one lane per (world, sphere)");
-    const int w = lane / NFOOT, s = lane % NFOOT;
-    float* fr = grp + (w < GW ? w : 0) * WFLOATS;
-    bool hit = false;
-    float cx = 0.f, cy = 0.f, pen = 0.f;
-    if (w < GW) {
-        const float* xs = fr + WL::XS + 8 * T.xslot[T.foot_body[s]];
-        const V3 c = add3(ld3(xs + 4), qrot(ld4(xs), ld3(T.foot_lpos + 3 * s)));
-        pen = c.z - G1M_FOOT_RADIUS;
-        hit = pen < 0.f;
-        cx = c.x; cy = c.y;
+    constexpr int WPP = 32 / G1_NFOOT_;  // worlds per pass
+    static_assert(WPP * G1_NFOOT_ == 32, "one lane per (world, sphere) in a pass");
+#pragma unroll 1
+    for (int w0 = 0; w0 < GW; w0 += WPP) {
+        const int wl = lane / NFOOT, w = w0 + wl, s = lane % NFOOT;
+        float* fr = grp + (w < GW ? w : 0) * WFLOATS;
+        bool hit = false;
+        float cx = 0.f, cy = 0.f, pen = 0.f;
+        if (w < GW) {
+            const float* xs = fr + WL::XS + 8 * T.xslot[T.foot_body[s]];
+            const V3 c = add3(ld3(xs + 4), qrot(ld4(xs), ld3(T.foot_lpos + 3 * s)));
+            pen = c.z - G1M_FOOT_RADIUS;
+            hit = pen < 0.f;
+            cx = c.x; cy = c.y;
+        }
+        const unsigned m = __ballot_sync(FULLMASK, hit);
+        const unsigned wm = (m >> (NFOOT * wl)) & ((1u << NFOOT) - 1u);
+        if (hit) {
+            const int k = __popc(wm & ((1u << s) - 1u));
+            int* con_s = reinterpret_cast<int*>(fr + WL::CON);
+            con_s[k] = s;
+            fr[WL::CON + 8 + 3 * k] = cx; fr[WL::CON + 9 + 3 * k] = cy; fr[WL::CON + 10 + 3 * k] = pen * 0.5f;
+            fr[WL::CON + 32 + k] = pen;
+        }
+        if (w < GW && s == 0) reinterpret_cast<int*>(fr + WL::MISC)[0] = __popc(wm);
     }
-    const unsigned m = __ballot_sync(FULLMASK, hit);
-    const unsigned wm = (m >> (NFOOT * (w < GW ? w : 0))) & ((1u << NFOOT) - 1u);
-    if (hit) {
-        const int k = __popc(wm & ((1u << s) - 1u));
-        int* con_s = reinterpret_cast<int*>(fr + WL::CON);
-        con_s[k] = s;
-        fr[WL::CON + 8 + 3 * k] = cx; fr[WL::CON + 9 + 3 * k] = cy; fr[WL::CON + 10 + 3 * k] = pen * 0.5f;
-        fr[WL::CON + 32 + k] = pen;
-    }
-    if (w < GW && s == 0) reinterpret_cast<int*>(fr + WL::MISC)[0] = __popc(wm);
     __syncwarp();
 }
 

@@ -139,6 +139,38 @@ __device__ __forceinline__ float obs_elem(int i, const float* qp, const float* q
     return i == 96 ? CMD_VX : 0.f;
 }
 
+// Raw observations k0 .. k0+7 (k0 % 8 == 0) of one world, the same values as obs_elem, with
+// every global load issued before the first is used (one L2 round trip per call instead of
+// one per element).
+__device__ __forceinline__ void obs8(int k0, const float* qp, const float* qv, const float* pa, const G1Tables& T,
+                                     float* o) {
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int i = k0 + j;
+        const float* src = i < 6 ? qv + i
+                         : i < 9 ? qp
+                         : i < 38 ? qp + T.act_qadr[i - 9]
+                         : i < 67 ? qv + T.act_dof[i - 38]
+                         : i < 96 ? pa + (i - 67) : nullptr;
+        x[j] = (src && (i < 6 || i >= 9)) ? *src : 0.f;
+    }
+    Q4 q = {0.f, 0.f, 0.f, 0.f};
+    if (k0 < 16) q = ld4(qp + 3);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int i = k0 + j;
+        if (i >= 6 && i < 9) {
+            float m[9];
+            qmat(q, m);
+            x[j] = -m[i];  // -third row of R_base
+        } else if (i >= 96) {
+            x[j] = i == 96 ? CMD_VX : 0.f;
+        }
+        o[j] = x[j];
+    }
+}
+
 // ------------------------------------------------------------------ policy phase
 // out[w][o] = act(b[o] + sum_i W[o][i] in[w][i]), i ascending (the mlp_forward order,
 // g1_env.cu:230-237), for the nw worlds of the block.  WT is [nin][wstr] (W transposed);
@@ -238,8 +270,8 @@ __device__ __noinline__ void cta_dense(const float* __restrict__ WT, int wstr, c
 // The block's actions go to A[t] (the physics phase reads them back from there).
 // k_rollout body, g1_env.cu:296-318.
 // final_value: only the value head is used (bootstrap Vlast, g1_env.cu:325-332).
-__device__ __forceinline__ void policy_sample(const Params& P, const float* HD, const float* lsp, int wbeg, int nbw,
-                                              int t, bool final_value);
+__device__ __forceinline__ void policy_sample(const Params& P, const float* HD, const float* lsp, float* tmp, int wbeg,
+                                              int nbw, int t, bool final_value);
 
 // tfs (shared memory, tensor-core path only): the g1tc::TfShared pipeline state (mbarriers,
 // TMEM address, phases), kept outside `work`, which the physics phases reuse.
@@ -273,16 +305,23 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
             const float* qp = P.qp + (size_t)gw * NQ;
             const float* qv = P.qv + (size_t)gw * NV;
             const float* pa = P.pa + (size_t)gw * NU;
-            float v[8], o[8];
+            float v[8], o[8], mu[8], va[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = k0 + j;
+                mu[j] = i < OBS_DIM ? P.mean[i] : 0.f;
+                va[j] = i < OBS_DIM ? P.var[i] : 0.f;
+            }
+            obs8(k0, qp, qv, pa, T, o);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int i = k0 + j;
                 float z = 0.f;
-                o[j] = 0.f;
                 if (i < OBS_DIM) {
-                    o[j] = obs_elem(i, qp, qv, pa, T);
-                    z = (o[j] - P.mean[i]) / sqrtf(P.var[i] + 1e-8f);
+                    z = (o[j] - mu[j]) / sqrtf(va[j] + 1e-8f);
                     if (z < -10.f) z = -10.f; else if (z > 10.f) z = 10.f;
+                } else {
+                    o[j] = 0.f;
                 }
                 v[j] = z;
             }
@@ -309,7 +348,7 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
                                      P.tf_err);
             PROF_MARK(l == 0 ? P_MLP : (l < P.nh ? P_MLP_L1 : P_MLP_HEAD));
         }
-        policy_sample(P, tf_hd, P.tf_bias + P.tf_lsoff, wbeg, nbw, t, final_value);
+        policy_sample(P, tf_hd, P.tf_bias + P.tf_lsoff, tf_hd + g1tc::TF_ROWS * 32, wbeg, nbw, t, final_value);
         PROF_MARK(P_SAMPLE);
         return;
     }
@@ -354,34 +393,39 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
     const float* lsp = wp + (size_t)nin * 32 + 32;
     __syncthreads();
     PROF_MARK(P_MLP_HEAD);
-    policy_sample(P, HD, lsp, wbeg, nbw, t, final_value);
+    policy_sample(P, HD, lsp, WTILE, wbeg, nbw, t, final_value);  // the weight tile is dead after the head
     PROF_MARK(P_SAMPLE);
 }
 
-// sampling: one thread per world, actions in index order (g1_env.cu:308-314); HD [nbw][32]
-// holds the 29 means and the value, lsp the 29 log-stds.
-__device__ __forceinline__ void policy_sample(const Params& P, const float* HD, const float* lsp, int wbeg, int nbw,
-                                              int t, bool final_value) {
+// sampling (g1_env.cu:308-318): one thread per (world, action) draws the Gaussian and writes
+// the action; the log-prob terms go to tmp [nbw][32] and one thread per world adds them in
+// action order.  HD [nbw][32] holds the 29 means and the value, lsp the 29 log-stds.
+__device__ __forceinline__ void policy_sample(const Params& P, const float* HD, const float* lsp, float* tmp, int wbeg,
+                                              int nbw, int t, bool final_value) {
+    const size_t sb0 = (size_t)t * P.N + wbeg;
+    if (!final_value) {
+        const float LOG2PI = 1.8378770664093453f;
+        const uint64_t tick = P.tick0 + (uint64_t)t;
+        for (int e = threadIdx.x; e < nbw * ACT_DIM; e += NTHREADS) {
+            const int w = e / ACT_DIM, i = e % ACT_DIM;
+            const uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)(wbeg + w), tick, RNG_ACTION, (uint32_t)i);
+            const float nz = sqrtf(-2.f * logf(u01_open(rb.x))) * cosf(6.283185307179586f * u01(rb.y));
+            const float ls = lsp[i];
+            P.A[sb0 * ACT_DIM + e] = HD[w * 32 + i] + expf(ls) * nz;
+            tmp[w * 32 + i] = -0.5f * nz * nz - ls - 0.5f * LOG2PI;
+        }
+        __syncthreads();
+    }
     if (threadIdx.x < nbw) {
         const int w = threadIdx.x, gw = wbeg + w;
         const float* hd = HD + w * 32;
         if (final_value) {
             P.Vlast[gw] = hd[29];
         } else {
-            const float LOG2PI = 1.8378770664093453f;
-            const uint64_t tick = P.tick0 + (uint64_t)t;
             float lps = 0.f;
-            const size_t sb = (size_t)t * P.N + gw;
-            for (int i = 0; i < ACT_DIM; ++i) {
-                uint4 rb = rng_draw(P.seed, P.world0 + (uint32_t)gw, tick, RNG_ACTION, (uint32_t)i);
-                float nz = sqrtf(-2.f * logf(u01_open(rb.x))) * cosf(6.283185307179586f * u01(rb.y));
-                float ls = lsp[i];
-                float a = hd[i] + expf(ls) * nz;
-                lps += -0.5f * nz * nz - ls - 0.5f * LOG2PI;
-                P.A[sb * ACT_DIM + i] = a;
-            }
-            P.LP[sb] = lps;
-            P.V[sb] = hd[29];
+            for (int i = 0; i < ACT_DIM; ++i) lps += tmp[w * 32 + i];
+            P.LP[sb0 + w] = lps;
+            P.V[sb0 + w] = hd[29];
         }
     }
     __syncthreads();
@@ -567,7 +611,8 @@ static_assert(((((int)((sizeof(G1Tables) + 15) / 16)) * 4 + NWARPS * GROUP_FLOAT
               "mbarriers need 8-byte alignment");
 // policy scratch of the tensor-core MLP inside the frames (g1_mlp_tc.cuh: activations,
 // weight stages, head outputs), 128 bytes of alignment slack
-static_assert(128 + g1tc::TF_SCRATCH <= NWARPS * GROUP_FLOATS * 4, "tensor-core MLP scratch must fit in the frames");
+static_assert(128 + g1tc::TF_SCRATCH + g1tc::TF_ROWS * 32 * 4 <= NWARPS * GROUP_FLOATS * 4,
+              "tensor-core MLP scratch and the sampling terms must fit in the frames");
 static_assert(sizeof(g1tc::TfShared) <= (16 + 2 * 16) * 4, "tensor-core MLP state must fit its smem slot");
 static_assert(MAX_WB * XSTR + 2 * MAX_WB * 260 + KT * OC <= NWARPS * GROUP_FLOATS, "MLP activations must fit in the frames");
 

@@ -110,6 +110,7 @@ struct Params {
     float *obs_out, *rew_out, *done_out;
     int* ncon_hist;  // [MAXCON+1] contact-count histogram (substeps), may be null
     int lockstep;    // > 0: the CTA's warps meet at a named barrier every `lockstep` substeps
+    int midbar;      // extra barriers inside a substep (group_qacc's midbar bits; with lockstep only)
     int* ncon_last;  // [N] contact count of each world's last substep (load balancing)
     int t0;          // trajectory row of the first control step of this launch
     int ext_policy;  // actions already in A[t0..]: skip the in-kernel policy phase
@@ -439,6 +440,13 @@ __device__ __forceinline__ void substep_barrier() { asm volatile("bar.sync 1, %0
 __device__ __forceinline__ void lockstep_barrier(const Params& P, int s) {
     if (P.lockstep > 0 && s % P.lockstep == 0) substep_barrier();
 }
+// the barriers group_qacc takes inside a substep, for a warp without a group this round
+__device__ __forceinline__ void idle_midbar(const Params& P) {
+    if (P.lockstep > 0) {
+        if (P.midbar & 1) substep_barrier();
+        if (P.midbar & 2) substep_barrier();
+    }
+}
 
 // One control step of GW worlds (global ids wid[0 .. nvalid-1]; the remaining slots carry a
 // stand pose and are not written back) by one warp: PD targets, S substeps, reward, done,
@@ -507,7 +515,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
 #endif
         PROF_MARK(P_BAR);
         int ncon[GW];
-        group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon);
+        group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon, nullptr, P.lockstep > 0 ? P.midbar : 0, NTHREADS);
         if (P.ncon_hist && lane == 0)
             for (int w = 0; w < nvalid; ++w) atomicAdd(&P.ncon_hist[ncon[w]], 1);
         if (s == P.S - 1 && P.ncon_last && lane < nvalid) {
@@ -689,7 +697,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
             }
             if (nvalid == 0) {
                 if (P.lockstep)
-                    for (int s = 0; s < P.S; ++s) lockstep_barrier(P, s);
+                    for (int s = 0; s < P.S; ++s) { lockstep_barrier(P, s); idle_midbar(P); }
                 continue;
             }
             const float* acts = P.mode == MODE_ROLLOUT ? P.A + (size_t)trow * P.N * ACT_DIM
@@ -1062,6 +1070,9 @@ static Params base_params(EnvState* E) {
     P.ncon_hist = E->ncon_hist;
     P.ncon_last = E->ncon_last;
     P.lockstep = getenv("G1_LOCKSTEP") ? atoi(getenv("G1_LOCKSTEP")) : 1;
+    // a second barrier per substep, after the contact solve (measured 0.8 % faster: the warps
+    // then integrate and start the next substep on the same code)
+    P.midbar = getenv("G1_MIDBAR") ? atoi(getenv("G1_MIDBAR")) : 2;
     // worlds per CTA: spread over all SMs, at most MAX_WB (then CTAs run in waves)
     int wb = (E->N + E->sm_count - 1) / E->sm_count;
     if (wb > 2 * GW * NWARPS) wb = 2 * GW * NWARPS;  // large N: blocks of two full rounds of groups

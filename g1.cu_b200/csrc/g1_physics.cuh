@@ -1042,10 +1042,14 @@ __device__ void group_smooth_detect(float* grp, const G1Tables& T, int lane, con
 // Full per-substep generalised acceleration for the GW worlds of the warp (qp, qv, tau
 // filled in each frame), the warp solving its own contact batches.  env_qacc.cuh:27-212.
 // qacc -> each frame's QACC; per-world outputs for k_qacc through the optional arrays.
+// midbar (fused rollout only): bit 0 -- the CTA's warps (bar_threads threads) meet at named
+// barrier 1 after the smooth dynamics, bit 1 -- after the contact solve.
 __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
-                           float* const* f_out, int* ncon_out, float* const* qs_out = nullptr) {
+                           float* const* f_out, int* ncon_out, float* const* qs_out = nullptr, int midbar = 0,
+                           int bar_threads = 0) {
     int ncon[GW];
     group_smooth_detect(grp, T, lane, opt, bias_out, ncon, qs_out);
+    if (midbar & 1) asm volatile("bar.sync 1, %0;" ::"r"(bar_threads) : "memory");
 #pragma unroll
     for (int w = 0; w < GW; ++w) {
         if (ncon_out) ncon_out[w] = ncon[w];
@@ -1067,6 +1071,7 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
                     f_out[B.wid[x]][lane] = lane < n4 ? cw[CL::FF + 4 * B.coff[x] + lane] : 0.f;
                 }
     }
+    if (midbar & 2) asm volatile("bar.sync 1, %0;" ::"r"(bar_threads) : "memory");
 }
 
 // ------------------------------------------------------------------ integration

@@ -233,6 +233,15 @@ __device__ __forceinline__ void body_ia_kept(const G1Tables& T, int b, const flo
     spatial_inertia21(Iw, ld3(bi + 6), T.body_mass[b], ia);
 }
 
+// F1's hand-off to its second pass for body b: orientation to qs[4], com offset and spatial
+// velocity to bi[9] (the body's kept-inertia row), spatial acceleration to f[6] (its force row)
+__device__ __forceinline__ void stash_body(float* qs, Q4 quat, V3 cpos, V3 w, V3 v, V3 aw, V3 av, float* f, float* bi) {
+    st4(qs, quat);
+    st3(bi, cpos); st3(bi + 3, w); st3(bi + 6, v);
+    st6(f, aw, av);
+}
+static_assert(4 * GW * NB <= CL::SIZE, "F1's orientation stash must fit in the contact workspace");
+
 // The smooth part of the per-substep dynamics for the GW worlds of a warp (qp, qv, tau in each
 // world frame): forward kinematics, motion axes S, RNE bias, the articulated-inertia factor
 // of M + dtB and qacc_smooth = (M + dtB)^-1 (-bias + tau) into QACC.
@@ -257,6 +266,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
     float *S = fr + WL::S, *BQ = fr + WL::BQ, *FOWN = fr + WL::FOWN, *UB = fr + WL::UB;
     float *FU = fr + WL::FU, *FINVD = fr + WL::FINVD, *qacc = fr + WL::QACC, *XS = fr + WL::XS;
     float* bias = (bias_out && w < GW) ? bias_out[w] : nullptr;
+    float* QS = grp + GW * WFLOATS;  // the group's contact workspace, idle until the contact solve
     PROF_BEGIN();
 
     // ---- floating base (body 1): the chain lanes of a world compute it redundantly
@@ -312,7 +322,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
             float* xs = XS + 8 * T.xslot[1];
             st4(xs, q1); st3(xs + 4, p);
             const V3 cpos = sub3(add3(p, qrot(q1, ld3(T.body_ipos + 3))), p);  // xipos - p, as the reference rounds it
-            body_force_keep(T, 1, q1, cpos, bw, bv, baw, bav, FOWN + 6, BQ + 9);
+            stash_body(QS + 4 * (w * NB + 1), q1, cpos, bw, bv, baw, bav, FOWN + 6, BQ + 9);
         }
     }
 
@@ -356,7 +366,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                 vv = {vv.x + sv.x * qd, vv.y + sv.y * qd, vv.z + sv.z * qd};
                 aw = {aw.x + sdw.x * qd, aw.y + sdw.y * qd, aw.z + sdw.z * qd};
                 av = {av.x + sdv.x * qd, av.y + sdv.y * qd, av.z + sdv.z * qd};
-                body_force_keep(T, b, quat, cpos, wv, vv, aw, av, FOWN + 6 * b, BQ + 9 * b);
+                stash_body(QS + 4 * (w * NB + b), quat, cpos, wv, vv, aw, av, FOWN + 6 * b, BQ + 9 * b);
                 if (T.branch_slot[b] >= 0) {
                     float* st = fr + WL::HF + 20 * T.branch_slot[b];
                     st3(st, pos); st4(st + 3, quat); st3(st + 7, wv); st3(st + 10, vv); st3(st + 13, aw); st3(st + 16, av);
@@ -365,6 +375,22 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
             __syncwarp();
         }
     }
+    // F1, second pass: the body forces and kept world inertias, one lane per (world, body),
+    // from the kinematics the chain walk stashed (in place: a body's stash sits in its own
+    // BQ / FOWN rows, its orientation in the idle contact workspace)
+#pragma unroll 1
+    for (int it = lane; it < GW * (NB - 1); it += 32) {
+        const int ww = it / (NB - 1), b = 1 + it % (NB - 1);
+        float* fw = grp + ww * WFLOATS;
+        float* bq = fw + WL::BQ + 9 * b;
+        float* fo = fw + WL::FOWN + 6 * b;
+        const Q4 quat = ld4(QS + 4 * (ww * NB + b));
+        const V3 cpos = ld3(bq), vw = ld3(bq + 3), vv = ld3(bq + 6);
+        const float2* f2 = reinterpret_cast<const float2*>(fo);
+        const float2 a01 = f2[0], a23 = f2[1], a45 = f2[2];
+        body_force_keep(T, b, quat, cpos, vw, vv, mk3(a01.x, a01.y, a23.x), mk3(a23.y, a45.x, a45.y), fo, bq);
+    }
+    __syncwarp();
     PROF_MARK(P_F1);
 
     // ---- B1: leaf -> root along the chains.  The contribution of the previous (child) body

@@ -233,11 +233,11 @@ __device__ __forceinline__ void body_ia_kept(const G1Tables& T, int b, const flo
     spatial_inertia21(Iw, ld3(bi + 6), T.body_mass[b], ia);
 }
 
-// F1's hand-off to its second pass for body b: orientation to qs[4], com offset and spatial
+// F1's hand-off to its second pass for body b: orientation to qs[4], position and spatial
 // velocity to bi[9] (the body's kept-inertia row), spatial acceleration to f[6] (its force row)
-__device__ __forceinline__ void stash_body(float* qs, Q4 quat, V3 cpos, V3 w, V3 v, V3 aw, V3 av, float* f, float* bi) {
+__device__ __forceinline__ void stash_body(float* qs, Q4 quat, V3 pos, V3 w, V3 v, V3 aw, V3 av, float* f, float* bi) {
     st4(qs, quat);
-    st3(bi, cpos); st3(bi + 3, w); st3(bi + 6, v);
+    st3(bi, pos); st3(bi + 3, w); st3(bi + 6, v);
     st6(f, aw, av);
 }
 static_assert(4 * GW * NB <= CL::SIZE, "F1's orientation stash must fit in the contact workspace");
@@ -321,8 +321,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
             for (int k = 0; k < 6; ++k) { st3(S + 6 * k, Sw[k]); st3(S + 6 * k + 3, Sv[k]); }
             float* xs = XS + 8 * T.xslot[1];
             st4(xs, q1); st3(xs + 4, p);
-            const V3 cpos = sub3(add3(p, qrot(q1, ld3(T.body_ipos + 3))), p);  // xipos - p, as the reference rounds it
-            stash_body(QS + 4 * (w * NB + 1), q1, cpos, bw, bv, baw, bav, FOWN + 6, BQ + 9);
+            stash_body(QS + 4 * (w * NB + 1), q1, p, bw, bv, baw, bav, FOWN + 6, BQ + 9);
         }
     }
 
@@ -356,7 +355,6 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                     float* xs = XS + 8 * T.xslot[b];
                     st4(xs, quat); st3(xs + 4, pos);
                 }
-                const V3 cpos = sub3(add3(pos, qrot(quat, ld3(T.body_ipos + 3 * b))), p);
                 const V3 sw = qrot(quat, ax);
                 const V3 sv = cross3(sub3(add3(pos, qrot(quat, an)), p), sw);
                 st6(S + 6 * d, sw, sv);
@@ -366,7 +364,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                 vv = {vv.x + sv.x * qd, vv.y + sv.y * qd, vv.z + sv.z * qd};
                 aw = {aw.x + sdw.x * qd, aw.y + sdw.y * qd, aw.z + sdw.z * qd};
                 av = {av.x + sdv.x * qd, av.y + sdv.y * qd, av.z + sdv.z * qd};
-                stash_body(QS + 4 * (w * NB + b), quat, cpos, wv, vv, aw, av, FOWN + 6 * b, BQ + 9 * b);
+                stash_body(QS + 4 * (w * NB + b), quat, pos, wv, vv, aw, av, FOWN + 6 * b, BQ + 9 * b);
                 if (T.branch_slot[b] >= 0) {
                     float* st = fr + WL::HF + 20 * T.branch_slot[b];
                     st3(st, pos); st4(st + 3, quat); st3(st + 7, wv); st3(st + 10, vv); st3(st + 13, aw); st3(st + 16, av);
@@ -385,7 +383,9 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
         float* bq = fw + WL::BQ + 9 * b;
         float* fo = fw + WL::FOWN + 6 * b;
         const Q4 quat = ld4(QS + 4 * (ww * NB + b));
-        const V3 cpos = ld3(bq), vw = ld3(bq + 3), vv = ld3(bq + 6);
+        // com offset xipos - p, rounded as the reference does it (the pelvis's pos is p itself)
+        const V3 cpos = sub3(add3(ld3(bq), qrot(quat, ld3(T.body_ipos + 3 * b))), ld3(fw + WL::QP));
+        const V3 vw = ld3(bq + 3), vv = ld3(bq + 6);
         const float2* f2 = reinterpret_cast<const float2*>(fo);
         const float2 a01 = f2[0], a23 = f2[1], a45 = f2[2];
         body_force_keep(T, b, quat, cpos, vw, vv, mk3(a01.x, a01.y, a23.x), mk3(a23.y, a45.x, a45.y), fo, bq);

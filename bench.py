@@ -239,6 +239,29 @@ def profile_case(h):
     print("profile case done")
 
 
+def profile_case3(h):
+    """Two g1_rollout calls of the config-3 workload (N = 32768, 100-1024-1024-512-29 ELU,
+    bf16 on the tensor cores) with horizon h: the small case for ncu captures of k_gemm."""
+    import torch
+    import g1env
+    N3 = 32768
+    env = g1env.G1Env(N3, S, PGS, seed=3)
+    env.set_policy((1024, 1024, 512), "elu", precision="bf16")
+    env.reset()
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (1024, 1024, 512), "elu"), seed=0).cuda()
+    W = g1env.pack_weights(ac).detach().contiguous()
+    mean, var = torch.zeros(100, device="cuda"), torch.ones(100, device="cuda")
+    z = lambda *sh: torch.zeros(*sh, device="cuda")
+    bufs = [z(h, N3, 100), z(h, N3, 29), z(h, N3), z(h, N3), z(h, N3), z(h, N3), z(N3)]
+    for _ in range(2):
+        env.rollout(h, W, mean, var, *bufs)
+    torch.cuda.synchronize()
+    if env.tc_status():
+        raise RuntimeError("tensor-core wait timed out in the config-3 rollout")
+    env.close()
+    print("profile case 3 done")
+
+
 def other_configs(dev):
     """Informational timings of BASELINE configs 1 and 3 on this GPU (CUDA events, L2 flushed
     between timed calls); the headline metric is config 2."""
@@ -312,7 +335,12 @@ def main():
     ap.add_argument("--no-other-configs", action="store_true")
     ap.add_argument("--profile-case", type=int, default=0, metavar="H",
                     help="run two H-step rollouts of the config-2 worlds and exit (small case for ncu captures)")
+    ap.add_argument("--profile-case3", type=int, default=0, metavar="H",
+                    help="run two H-step rollouts of the config-3 workload and exit (small case for ncu captures)")
     args = ap.parse_args()
+    if args.profile_case3:
+        profile_case3(args.profile_case3)
+        return
     if args.profile_case:
         profile_case(args.profile_case)
         return

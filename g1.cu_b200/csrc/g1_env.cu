@@ -1164,7 +1164,7 @@ static cudaError_t launch_gemm_tma(int M, int N, int K, const __nv_bfloat16* X, 
     if (!make_map(&mx, X, K, M, ldx, g1gemm::BM) || !make_map(&mw, W, K, N, K, BN)) return cudaErrorInvalidValue;
     const int tiles = ((M + g1gemm::BM - 1) / g1gemm::BM) * ((N + BN - 1) / BN);
     const int grid = tiles < nsm ? tiles : nsm;
-    g1gemm::k_gemm<BN><<<grid, g1gemm::NTH, smem, stream>>>(mx, mw, M, N, K, bias, act, ob, of, of ? ldo : ldob, err);
+    g1gemm::k_gemm<BN><<<grid, g1gemm::nth<BN>(), smem, stream>>>(mx, mw, M, N, K, bias, act, ob, of, of ? ldo : ldob, err);
     return cudaGetLastError();
 }
 

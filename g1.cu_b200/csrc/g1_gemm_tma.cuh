@@ -11,8 +11,9 @@
 //   directly (8-row groups 1024 bytes apart; the 16-wide K steps 32 bytes apart inside the
 //   swizzle atom).
 // * Warp 0 lane 0 issues the loads; warp 1 lane 0 issues `tcgen05.mma.cta_group::1.kind::f16`
-//   (M = 128, N = BN, K = 16) and commits each stage to its `empty` barrier; warps 2..9 run
-//   the epilogue (two per TMEM lane quarter, each half of the columns): `tcgen05.ld`, bias,
+//   (M = 128, N = BN, K = 16) and commits each stage to its `empty` barrier; the other warps
+//   run the epilogue (four per TMEM lane quarter for BN >= 128, two otherwise, each on an
+//   equal share of the columns): `tcgen05.ld`, bias,
 //   activation, store.  The accumulator is double-buffered in TMEM (2 x BN columns) so the
 //   epilogue of one tile overlaps the MMAs of the next.
 // * Every mbarrier wait is bounded; a timeout sets *err and the CTA stops waiting (results are
@@ -25,7 +26,13 @@
 
 namespace g1gemm {
 
-constexpr int BM = 128, BK = 64, STAGES = 4, NEPI = 8, NTH = 64 + 32 * NEPI;
+constexpr int BM = 128, BK = 64, STAGES = 4;
+// epilogue warps: four per TMEM lane quarter for wide tiles (each a quarter of the columns),
+// two for narrow ones
+template <int BN>
+__host__ __device__ constexpr int nepi() { return BN >= 128 ? 16 : 8; }
+template <int BN>
+__host__ __device__ constexpr int nth() { return 64 + 32 * nepi<BN>(); }
 constexpr uint32_t SPIN = 1u << 22;
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -75,7 +82,7 @@ constexpr int smem_bytes() {
 
 // act: 0 tanh, 1 ELU, -1 identity; out_b (bf16, ld ldo) or out_f (fp32, ld ldo)
 template <int BN>
-__global__ void __launch_bounds__(NTH, 1)
+__global__ void __launch_bounds__(nth<BN>(), 1)
 k_gemm(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, int M, int N, int K,
        const float* __restrict__ bias, int act, __nv_bfloat16* __restrict__ out_b, float* __restrict__ out_f, int ldo,
        int* err) {
@@ -90,7 +97,7 @@ k_gemm(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensor
         }
         for (int i = 0; i < 2; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s32(&S.tfull[i])));
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s32(&S.tempty[i])), "r"(NEPI));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s32(&S.tempty[i])), "r"(nepi<BN>()));
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -154,9 +161,10 @@ k_gemm(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensor
                          : "memory");
             if (++acc == 2) { acc = 0; accph ^= 1u; }
         }
-    } else if (warp >= 2) {  // epilogue: warp w reads TMEM lanes 32 (w & 3) .., half (w - 2) / 4 of the columns
+    } else if (warp >= 2) {  // epilogue: warp w reads TMEM lanes 32 (w & 3) .., part (w - 2) / 4 of the columns
         const int q = warp & 3, half = (warp - 2) >> 2;
-        constexpr int CW = BN / 2;  // columns per epilogue warp
+        constexpr int CW = BN / (nepi<BN>() / 4);  // columns per epilogue warp
+        static_assert(CW % 16 == 0, "16-column TMEM loads");
         uint32_t acc = 0, accph = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             const int m0 = (tile % ntm) * BM, n0 = (tile / ntm) * BN;

@@ -630,7 +630,7 @@ __device__ __forceinline__ void load_tables(float* smem) {
     for (int i = threadIdx.x; i < (int)(sizeof(G1Tables) / 16); i += blockDim.x) dst[i] = src[i];
 }
 
-__global__ void __launch_bounds__(NTHREADS, 1) k_g1(Params P) {
+__global__ void __launch_bounds__(NTHREADS, 1) k_g1(const __grid_constant__ Params P) {
 #ifdef G1_PROF
     const long long t_kernel0 = clock64();
 #endif

@@ -830,13 +830,34 @@ __device__ void group_detect(float* grp, const G1Tables& T, int lane) {
 
 // A contact batch: worlds of the group (slot ids) whose contacts are solved together,
 // at most MAXCON contacts in total; contact gc of the batch belongs to world slot
-// wid[x] with coff[x] <= gc < coff[x+1].
+// wid[x] with coff[x] <= gc < coff[x+1].  The accessors index with unrolled selects, so a
+// batch lives in registers (a run-time array index would put it in local memory).
 struct Batch {
     int nw, wid[GW], coff[GW + 1];
     __device__ __forceinline__ int world_of(int gc) const {
         int x = 0;
-        while (x + 1 < nw && gc >= coff[x + 1]) ++x;
+#pragma unroll
+        for (int k = 1; k < GW; ++k) x += (k < nw && gc >= coff[k]) ? 1 : 0;
         return x;
+    }
+    __device__ __forceinline__ int wof(int x) const {
+        int r = wid[0];
+#pragma unroll
+        for (int k = 1; k < GW; ++k) r = (x == k) ? wid[k] : r;
+        return r;
+    }
+    __device__ __forceinline__ int cof(int x) const {
+        int r = coff[0];
+#pragma unroll
+        for (int k = 1; k <= GW; ++k) r = (x == k) ? coff[k] : r;
+        return r;
+    }
+    // appends world slot w with n contacts
+    __device__ __forceinline__ void append(int w, int n) {
+#pragma unroll
+        for (int k = 0; k < GW; ++k)
+            if (k == nw) { wid[k] = w; coff[k + 1] = coff[k] + n; }
+        ++nw;
     }
 };
 
@@ -845,17 +866,17 @@ struct Batch {
 // by side; the Delassus matrix is block diagonal over worlds and each world's PGS sweeps
 // its own rows in order, all worlds in the same pass.  f -> cw[FF] (world x's rows start at
 // 4*coff[x]).
-__device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, const Batch& B) {
+__device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, const Batch B) {
     float* MM = cw + CL::MM;
     float* EB = cw + CL::EB;
-    const int nc = B.coff[B.nw], nb = 3 * nc, nefc_all = 4 * nc;
+    const int nc = B.cof(B.nw), nb = 3 * nc, nefc_all = 4 * nc;
     PROF_BEGIN();
     for (int e = lane; e < nb * MSTR; e += 32) MM[e] = 0.f;
     __syncwarp();
     // basis rows e0 = n, e1 = mu t1, e2 = mu t2 over the ancestor dofs (env_qacc.cuh:113-126)
     for (int it = lane; it < nc * CDS; it += 32) {
-        const int gc = it / CDS, k = it % CDS, x = B.world_of(gc), c = gc - B.coff[x];
-        const float* fr = grp + B.wid[x] * WFLOATS;
+        const int gc = it / CDS, k = it % CDS, x = B.world_of(gc), c = gc - B.cof(x);
+        const float* fr = grp + B.wof(x) * WFLOATS;
         const int s = reinterpret_cast<const int*>(fr + WL::CON)[c];
         if (k < T.foot_ndof[s]) {
             const int a = T.foot_dofs[s][k];
@@ -872,8 +893,8 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     PROF_MARK(P_CSETUP);
     if (lane < nb) {
         const int gc = lane / 3, x = B.world_of(gc);
-        const float* fr = grp + B.wid[x] * WFLOATS;
-        const int s = reinterpret_cast<const int*>(fr + WL::CON)[gc - B.coff[x]];
+        const float* fr = grp + B.wof(x) * WFLOATS;
+        const int s = reinterpret_cast<const int*>(fr + WL::CON)[gc - B.cof(x)];
         lane_solve(fr, T, MM + lane * MSTR, cw + CL::GRAM + lane * SOLVE_SCRATCH, T.foot_chains[s]);
     }
     __syncwarp();
@@ -881,8 +902,8 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     // per contact: bb = e.qacc_smooth, e.qvel -> R, aref, b  (env_qacc.cuh:113-136, 188-191)
     float *RR = cw + CL::RR, *BV = cw + CL::BV;
     if (lane < nc) {
-        const int gc = lane, x = B.world_of(gc), c = gc - B.coff[x];
-        const float* fr = grp + B.wid[x] * WFLOATS;
+        const int gc = lane, x = B.world_of(gc), c = gc - B.cof(x);
+        const float* fr = grp + B.wof(x) * WFLOATS;
         const int s = reinterpret_cast<const int*>(fr + WL::CON)[c], nd = T.foot_ndof[s];
         const float *qs = fr + WL::QACC, *qv = fr + WL::QV;
         float b0 = 0, b1 = 0, b2 = 0, v0 = 0, v1 = 0, v2 = 0;
@@ -914,21 +935,33 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     poff[0] = 0;
 #pragma unroll
     for (int x = 0; x < GW; ++x) {
-        const int n = x < B.nw ? B.coff[x + 1] - B.coff[x] : 0;
+        const int n = x < B.nw ? B.cof(x + 1) - B.cof(x) : 0;
         poff[x + 1] = poff[x] + n * (n + 1) / 2;
     }
-    const int npair = poff[B.nw];
+    auto pof = [&](int x) {
+        int r = poff[0];
+#pragma unroll
+        for (int k = 1; k <= GW; ++k) r = (x == k) ? poff[k] : r;
+        return r;
+    };
+    // the world of pair pr: count the worlds whose pairs start at or before it
+    auto pair_world = [&](int pr) {
+        int x = 0;
+#pragma unroll
+        for (int k = 1; k < GW; ++k) x += (k < B.nw && pr >= poff[k]) ? 1 : 0;
+        return x;
+    };
+    const int npair = pof(B.nw);
     // 3x3 Gram blocks G[a][b] = e_{c,a} . m_{c',b} over c's dofs (env_qacc.cuh:161-171)
     float* G = cw + CL::GRAM;
     for (int it = lane; it < npair * 9; it += 32) {
         const int pr = it / 9, ab = it % 9, a = ab / 3, bb = ab % 3;
-        int x = 0;
-        while (x + 1 < B.nw && pr >= poff[x + 1]) ++x;
-        const int n = B.coff[x + 1] - B.coff[x];
-        int c = 0, rem = pr - poff[x];
+        const int x = pair_world(pr);
+        const int n = B.cof(x + 1) - B.cof(x);
+        int c = 0, rem = pr - pof(x);
         while (rem >= n - c) { rem -= n - c; ++c; }
-        const int gc = B.coff[x] + c, gcp = B.coff[x] + c + rem;
-        const float* fr = grp + B.wid[x] * WFLOATS;
+        const int gc = B.cof(x) + c, gcp = B.cof(x) + c + rem;
+        const float* fr = grp + B.wof(x) * WFLOATS;
         const int s = reinterpret_cast<const int*>(fr + WL::CON)[c], nd = T.foot_ndof[s];
         const float* ea = EB + gc * 36 + 12 * a;
         const float* mcp = MM + (3 * gcp + bb) * MSTR;
@@ -942,10 +975,9 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     float* AP = cw + CL::AP;
     for (int it = lane; it < npair * 4; it += 32) {
         const int pr = it >> 2, k = it & 3;
-        int x = 0;
-        while (x + 1 < B.nw && pr >= poff[x + 1]) ++x;
-        const int n = B.coff[x + 1] - B.coff[x];
-        int c = 0, rem = pr - poff[x];
+        const int x = pair_world(pr);
+        const int n = B.cof(x + 1) - B.cof(x);
+        int c = 0, rem = pr - pof(x);
         while (rem >= n - c) { rem -= n - c; ++c; }
         const int cp = c + rem;
         const float* g = G + 9 * pr;
@@ -953,14 +985,14 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
         const float t0 = c0 * g[0] + c1 * g[3] + c2 * g[6];
         const float t1 = c0 * g[1] + c1 * g[4] + c2 * g[7];
         const float t2 = c0 * g[2] + c1 * g[5] + c2 * g[8];
-        const int i = 4 * (B.coff[x] + c) + k;
+        const int i = 4 * (B.cof(x) + c) + k;
         // inside a diagonal block the reference's later (larger k) write of (k,kp)/(kp,k) wins
         const int kpmax = (c == cp) ? k : 3;
 #pragma unroll
         for (int kp = 0; kp < 4; ++kp) {
             if (kp > kpmax) break;
             float aij = t0 * dcoef(kp, 0) + t1 * dcoef(kp, 1) + t2 * dcoef(kp, 2);
-            const int j = 4 * (B.coff[x] + cp) + kp;
+            const int j = 4 * (B.cof(x) + cp) + kp;
             if (i == j) aij += RR[i];
             AP[apidx(i, j)] = aij;
         }
@@ -971,11 +1003,11 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     // by side.  Lane j keeps the residual r_j = b_j + sum_k A_jk f_k of its row; after row i of
     // its world moves by delta, it adds A_ji delta.
     const int xj = lane < nefc_all ? B.world_of(lane / 4) : 0;
-    const int r0 = 4 * B.coff[xj], nrow = lane < nefc_all ? 4 * (B.coff[xj + 1] - B.coff[xj]) : 0;
+    const int r0 = 4 * B.cof(xj), nrow = lane < nefc_all ? 4 * (B.cof(xj + 1) - B.cof(xj)) : 0;
     int maxrow = 0;
 #pragma unroll
     for (int x = 0; x < GW; ++x)
-        if (x < B.nw) maxrow = max(maxrow, 4 * (B.coff[x + 1] - B.coff[x]));
+        if (x < B.nw) maxrow = max(maxrow, 4 * (B.cof(x + 1) - B.cof(x)));
     float fj = 0.f, rj = lane < nefc_all ? BV[lane] : 0.f;
     const float ajj = lane < nefc_all ? AP[apidx(lane, lane)] : 1.f;
     const float inv = 1.f / ajj;
@@ -1012,9 +1044,9 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     // qacc = qacc_smooth + sum_c sum_a fb_c[a] m_{c,a}, per world  (env_qacc.cuh:199-211)
     for (int it = lane; it < B.nw * NV; it += 32) {
         const int x = it / NV, d = it % NV;
-        float* qacc = grp + B.wid[x] * WFLOATS + WL::QACC;
+        float* qacc = grp + B.wof(x) * WFLOATS + WL::QACC;
         float dq = 0.f;
-        for (int gc = B.coff[x]; gc < B.coff[x + 1]; ++gc) {
+        for (int gc = B.cof(x); gc < B.cof(x + 1); ++gc) {
             const float f0 = F[4 * gc], f1 = F[4 * gc + 1], f2 = F[4 * gc + 2], f3 = F[4 * gc + 3];
             const float fb0 = f0 + f1 + f2 + f3, fb1 = f0 - f1, fb2 = f2 - f3;
             const float* mc = MM + 3 * gc * MSTR;
@@ -1024,29 +1056,6 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     }
     __syncwarp();
     PROF_MARK(P_DQ);
-}
-
-// Contact batches of the group's worlds: greedy in slot order, at most MAXCON contacts per
-// batch (worlds without contacts are skipped).  Returns the number of batches.
-__device__ __forceinline__ int form_batches(const int* ncon, Batch* out) {
-    int nb = 0;
-    Batch B;
-    B.nw = 0;
-    B.coff[0] = 0;
-#pragma unroll 1
-    for (int w = 0; w <= GW; ++w) {
-        const bool flush = (w == GW) ? B.nw > 0 : (ncon[w] > 0 && B.coff[B.nw] + ncon[w] > MAXCON);
-        if (flush) {
-            out[nb++] = B;
-            B.nw = 0;
-        }
-        if (w < GW && ncon[w] > 0) {
-            B.wid[B.nw] = w;
-            B.coff[B.nw + 1] = B.coff[B.nw] + ncon[w];
-            ++B.nw;
-        }
-    }
-    return nb;
 }
 
 // Smooth dynamics and contact detection for the GW worlds of the warp; ncon per world.
@@ -1081,22 +1090,35 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
         if (ncon_out) ncon_out[w] = ncon[w];
         if (f_out && f_out[w] && ncon[w] == 0) f_out[w][lane] = 0.f;
     }
-    Batch bs[GW];
-    const int nb = form_batches(ncon, bs);
-#pragma unroll 1
-    for (int i = 0; i < nb; ++i) {
-        const Batch& B = bs[i];
+    // contact batches, formed greedily in slot order (at most MAXCON contacts each; worlds
+    // without contacts skipped) and solved as they close
+    auto solve = [&](const Batch& B) {
 #ifdef G1_PROF
-        if (lane == 0) atomicAdd(&g_prof[47 + B.coff[B.nw]], 1ull);  // batches by contact count 1..8
+        if (lane == 0) atomicAdd(&g_prof[47 + B.cof(B.nw)], 1ull);  // batches by contact count 1..8
 #endif
         batch_contact(grp, cw, T, lane, opt, B);
         if (f_out)
-            for (int x = 0; x < B.nw; ++x)
-                if (f_out[B.wid[x]]) {
-                    const int n4 = 4 * (B.coff[x + 1] - B.coff[x]);
-                    f_out[B.wid[x]][lane] = lane < n4 ? cw[CL::FF + 4 * B.coff[x] + lane] : 0.f;
+#pragma unroll
+            for (int x = 0; x < GW; ++x)
+                if (x < B.nw && f_out[B.wof(x)]) {
+                    const int n4 = 4 * (B.cof(x + 1) - B.cof(x));
+                    f_out[B.wof(x)][lane] = lane < n4 ? cw[CL::FF + 4 * B.cof(x) + lane] : 0.f;
                 }
+    };
+    Batch B;
+    B.nw = 0;
+    B.coff[0] = 0;
+#pragma unroll
+    for (int w = 0; w < GW; ++w) {
+        if (ncon[w] > 0) {
+            if (B.cof(B.nw) + ncon[w] > MAXCON) {
+                solve(B);
+                B.nw = 0;
+            }
+            B.append(w, ncon[w]);
+        }
     }
+    if (B.nw > 0) solve(B);
     if (midbar & 2) asm volatile("bar.sync 1, %0;" ::"r"(bar_threads) : "memory");
 }
 

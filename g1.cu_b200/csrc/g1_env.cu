@@ -448,12 +448,29 @@ __device__ __forceinline__ void idle_midbar(const Params& P) {
     }
 }
 
+// The global world ids of a group's GW slots.  Indexed through unrolled selects, so the ids
+// stay in registers (a run-time array index would put them in local memory).
+struct Slots {
+    int v[GW];
+    __device__ __forceinline__ int operator[](int w) const {
+        int r = v[0];
+#pragma unroll
+        for (int k = 1; k < GW; ++k) r = (w == k) ? v[k] : r;
+        return r;
+    }
+    __device__ __forceinline__ void set(int w, int id) {
+#pragma unroll
+        for (int k = 0; k < GW; ++k)
+            if (k == w) v[k] = id;
+    }
+};
+
 // One control step of GW worlds (global ids wid[0 .. nvalid-1]; the remaining slots carry a
 // stand pose and are not written back) by one warp: PD targets, S substeps, reward, done,
 // auto-reset.  env_advance, g1_env.cu:118-212.  `acts_base`: actions indexed by global world
 // id (row-major [N,29]; null = zero action).
-__device__ void group_control_step(const Params& P, const G1Tables& T, float* grp, float* cw, const int* wid, int nvalid,
-                                   const float* acts_base, uint64_t tick, float* r_out, float* d_out) {
+__device__ void group_control_step(const Params& P, const G1Tables& T, float* grp, float* cw, const Slots& wid, int nvalid,
+                                   const float* acts_base, uint64_t tick, float& r_out, float& d_out) {
     const int lane = threadIdx.x & 31;
     PROF_BEGIN();
     // slot w < nvalid holds world wid[w]; its actions are acts_base[wid[w]] (null = zero)
@@ -477,11 +494,8 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
         grp[w * WFLOATS + WL::TGT + i] = t;
     }
     float energy = 0.f, vx_sum = 0.f;  // lane w < GW: world w
-    const float* bdt_all[GW];
-#pragma unroll
-    for (int w = 0; w < GW; ++w) bdt_all[w] = T.bdt;
     QaccOpts opt;
-    opt.pgs_iters = P.pgs; opt.mu = P.mu; opt.bdt = bdt_all;
+    opt.pgs_iters = P.pgs; opt.mu = P.mu; opt.bdt = nullptr; opt.bdt_all = T.bdt;
     PROF_MARK(P_CS_LOAD);
     // PD torque, clamped to the actuator range, and |tau qd| accumulated into the energy
     // actuator by actuator in index order (g1_env.cu:143-152).  The torque of substep s + 1 is
@@ -517,7 +531,9 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
         int ncon[GW];
         group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon, nullptr, P.lockstep > 0 ? P.midbar : 0, NTHREADS);
         if (P.ncon_hist && lane == 0)
-            for (int w = 0; w < nvalid; ++w) atomicAdd(&P.ncon_hist[ncon[w]], 1);
+#pragma unroll
+            for (int w = 0; w < GW; ++w)
+                if (w < nvalid) atomicAdd(&P.ncon_hist[ncon[w]], 1);
         if (s == P.S - 1 && P.ncon_last && lane < nvalid) {
             int nc = 0;
 #pragma unroll
@@ -565,8 +581,8 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
         if (won) r += FINISH_BONUS;
         d_flag = (!alive || won || step >= 1000) ? 1 : 0;
         P.steps[gw] = d_flag ? 0 : step;
-        r_out[w] = r;
-        d_out[w] = (float)d_flag;
+        r_out = r;
+        d_out = (float)d_flag;
     }
     unsigned dmask = __ballot_sync(FULLMASK, d_flag != 0);
     __syncwarp();
@@ -687,13 +703,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(const __grid_constant__ Para
         PROF_MARK(P_SORT);
         for (int round = 0; round < nrounds; ++round) {
             const int g = warp + round * NWARPS;
-            int wid[GW];
+            Slots wid;
             int nvalid = 0;
 #pragma unroll
             for (int sl = 0; sl < GW; ++sl) {
                 const int pidx = sl * ngroups + ((sl & 1) ? ngroups - 1 - g : g);
-                wid[sl] = wbeg;
-                if (g < ngroups && pidx < nbw) wid[nvalid++] = wbeg + perm[pidx];
+                wid.v[sl] = wbeg;
+                if (g < ngroups && pidx < nbw) wid.set(nvalid++, wbeg + perm[pidx]);
             }
             if (nvalid == 0) {
                 if (P.lockstep)
@@ -702,13 +718,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(const __grid_constant__ Para
             }
             const float* acts = P.mode == MODE_ROLLOUT ? P.A + (size_t)trow * P.N * ACT_DIM
                               : P.act_in;  // MODE_STEP: this step's actions; MODE_PHYS: constant actions (may be null = zero)
-            float r[GW], d[GW];
-            group_control_step(P, T, grp, cw, wid, nvalid, acts, tick, r, d);
-            int my_w = 0;
-            float my_r = 0.f, my_d = 0.f;
-#pragma unroll
-            for (int sl = 0; sl < GW; ++sl)
-                if (sl == lane) { my_w = wid[sl]; my_r = r[sl]; my_d = d[sl]; }
+            float my_r = 0.f, my_d = 0.f;  // lane w < nvalid: reward and done of slot w
+            group_control_step(P, T, grp, cw, wid, nvalid, acts, tick, my_r, my_d);
+            const int my_w = wid[lane < GW ? lane : 0];
             if (lane < nvalid) {
                 if (P.mode == MODE_ROLLOUT) {
                     P.R[(size_t)trow * P.N + my_w] = my_r;
@@ -722,9 +734,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_g1(const __grid_constant__ Para
                 __syncwarp();
                 for (int it = lane; it < nvalid * OBS_DIM; it += 32) {
                     const int sl = it / OBS_DIM, i = it % OBS_DIM;
-                    int gw = wid[0];
-#pragma unroll
-                    for (int q = 1; q < GW; ++q) gw = (q == sl) ? wid[q] : gw;
+                    const int gw = wid[sl];
                     P.obs_out[(size_t)gw * OBS_DIM + i] =
                         obs_elem(i, P.qp + (size_t)gw * NQ, P.qv + (size_t)gw * NV, P.pa + (size_t)gw * NU, T);
                 }
@@ -782,7 +792,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_qacc(int n, const float* qpos, 
             qs_w[w] = (ok && qacc_s_out) ? qacc_s_out + (size_t)(s0 + w) * NV : nullptr;
         }
         QaccOpts opt;
-        opt.pgs_iters = pgs; opt.mu = mu; opt.bdt = bdt_w;
+        opt.pgs_iters = pgs; opt.mu = mu; opt.bdt = bdt_w; opt.bdt_all = nullptr;
         int ncon[GW];
         group_qacc(grp, cw, T, lane, opt, bias_w, f_w, ncon, qs_w);
         for (int it = lane; it < nvalid * NV; it += 32) {

@@ -257,9 +257,16 @@ static_assert(4 * GW * NB <= CL::SIZE, "F1's orientation stash must fit in the c
 //   base: the floating base's 6x6 block, its Cholesky solve (aba_factor.cuh:90-108,138-155);
 //   F2 (root->leaf): qdd per hinge body (aba_factor.cuh:156-164).
 // bias_out (optional, per world slot, global memory) receives qfrc_bias.
-__device__ void group_smooth(float* grp, const G1Tables& T, int lane, const float* const* bdt_w, float* const* bias_out) {
+__device__ void group_smooth(float* grp, const G1Tables& T, int lane, const float* const* bdt_w, float* const* bias_out,
+                             const float* bdt_all = nullptr) {
     const int w = lane >> 2, cl = lane & 3;
-    const float* bdt = (bdt_w && w < GW) ? bdt_w[w] : nullptr;
+    const float* bdt = nullptr;  // world w's entry, by unrolled select (no run-time index)
+    if (bdt_all) {
+        bdt = w < GW ? bdt_all : nullptr;
+    } else if (bdt_w && w < GW) {
+#pragma unroll
+        for (int k = 0; k < GW; ++k) bdt = (w == k) ? bdt_w[k] : bdt;
+    }
     const bool on = w < GW && cl < T.nchain;
     float* fr = grp + (w < GW ? w : 0) * WFLOATS;
     const float *qp = fr + WL::QP, *qv = fr + WL::QV, *tau = fr + WL::TAU;
@@ -794,6 +801,7 @@ struct QaccOpts {
     int pgs_iters;
     float mu;
     const float* const* bdt;  // per world slot: shared-memory dt*B diagonal (entries may be null)
+    const float* bdt_all;     // if non-null: the dt*B diagonal of every world slot (bdt unused)
 };
 
 // Foot-sphere contacts of the GW worlds (contact.cuh:31-46), lane = 8 (w - w0) + sphere in
@@ -1061,7 +1069,7 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
 // Smooth dynamics and contact detection for the GW worlds of the warp; ncon per world.
 __device__ void group_smooth_detect(float* grp, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
                                     int* ncon, float* const* qs_out = nullptr) {
-    group_smooth(grp, T, lane, opt.bdt, bias_out);
+    group_smooth(grp, T, lane, opt.bdt, bias_out, opt.bdt_all);
     PROF_BEGIN();
     if (qs_out)
         for (int it = lane; it < GW * NV; it += 32) {

@@ -874,7 +874,8 @@ struct Batch {
 // by side; the Delassus matrix is block diagonal over worlds and each world's PGS sweeps
 // its own rows in order, all worlds in the same pass.  f -> cw[FF] (world x's rows start at
 // 4*coff[x]).
-__device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, const Batch B) {
+__device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, int pgs_iters, float mu,
+                                          const Batch B) {
     float* MM = cw + CL::MM;
     float* EB = cw + CL::EB;
     const int nc = B.cof(B.nw), nb = 3 * nc, nefc_all = 4 * nc;
@@ -892,7 +893,7 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
             const V3 p = ld3(fr + WL::XS + 8 * T.xslot[1] + 4);
             const V3 r = sub3(ld3(fr + WL::CON + 8 + 3 * c), p);
             const V3 t = add3(cross3(ld3(S + 6 * a), r), ld3(S + 6 * a + 3));
-            const float e0 = t.z, e1 = opt.mu * t.y, e2 = -opt.mu * t.x;
+            const float e0 = t.z, e1 = mu * t.y, e2 = -mu * t.x;
             EB[gc * 36 + k] = e0; EB[gc * 36 + 12 + k] = e1; EB[gc * 36 + 24 + k] = e2;
             MM[(3 * gc) * MSTR + a] = e0; MM[(3 * gc + 1) * MSTR + a] = e1; MM[(3 * gc + 2) * MSTR + a] = e2;
         }
@@ -925,7 +926,7 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
         const float dmax = T.solimp[1], tc = T.solref[0], dr = T.solref[1];
         const float bcoef = 2.f / (dmax * tc);
         const float kcoef = 1.f / (dmax * dmax * tc * tc * dr * dr);
-        const float pyr = (1.f + opt.mu * opt.mu) * (2.f * opt.mu * opt.mu / G1M_FOOT_IMPRATIO);
+        const float pyr = (1.f + mu * mu) * (2.f * mu * mu / G1M_FOOT_IMPRATIO);
         const float pn = fr[WL::CON + 32 + c], imp = foot_impedance(T, pn);
         const float Rc = T.foot_invw0[s] * pyr * (1.f - imp) / imp;
         const float kip = kcoef * imp * pn;
@@ -1027,7 +1028,7 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
         if (i >= maxrow) break;  // rows past the batch's largest world are never read
         acol[i] = i < nrow ? AP[apidx(r0 + i, lane)] : 0.f;
     }
-    for (int itr = 0; itr < opt.pgs_iters; ++itr) {
+    for (int itr = 0; itr < pgs_iters; ++itr) {
 #pragma unroll
         for (int i = 0; i < 4 * MAXCON; ++i) {
             if (i >= maxrow) break;
@@ -1104,7 +1105,7 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
 #ifdef G1_PROF
         if (lane == 0) atomicAdd(&g_prof[47 + B.cof(B.nw)], 1ull);  // batches by contact count 1..8
 #endif
-        batch_contact(grp, cw, T, lane, opt, B);
+        batch_contact(grp, cw, T, lane, opt.pgs_iters, opt.mu, B);
         if (f_out)
 #pragma unroll
             for (int x = 0; x < GW; ++x)

@@ -529,7 +529,7 @@ __device__ void group_control_step(const Params& P, const G1Tables& T, float* gr
 #endif
         PROF_MARK(P_BAR);
         int ncon[GW];
-        group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon, nullptr, P.lockstep > 0 ? P.midbar : 0, NTHREADS);
+        group_qacc(grp, cw, T, lane, opt, nullptr, nullptr, ncon, nullptr, P.lockstep > 0 ? P.midbar : 0, NTHREADS, 1);
         if (P.ncon_hist && lane == 0)
 #pragma unroll
             for (int w = 0; w < GW; ++w)

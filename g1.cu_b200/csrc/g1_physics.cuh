@@ -151,8 +151,7 @@ struct WL {  // per-world frame, offsets in floats
         BQ = 708,             // per body (F1 -> B1): world rotational inertia, upper triangle
                               // [xx xy xz yy yz zz], then xipos - p [3]
         FOWN = BQ + 280,      // per body: own force, then subtree force [31][6]
-        UB = FOWN + 186,      // per body: u_b [31] (+1)
-        HF = UB + 32,         // F1 branch hand-off: pos, quat, w, v, aw, av [19] (+1) per branch slot
+        HF = FOWN + 186,      // F1 branch hand-off: pos, quat, w, v, aw, av [19] (+1) per branch slot
         HA = HF + 20 * G1_MAXBRANCH,   // F2 branch hand-off: spatial acceleration [6] (+2)
         HB = HA + 8 * G1_MAXBRANCH,    // B1 chain-head contributions: IA [21], f [6], pA [6] (+3)
         A1 = HB + 36 * 4,     // base spatial acceleration [6] (+2)
@@ -257,8 +256,9 @@ static_assert(4 * GW * NB <= CL::SIZE, "F1's orientation stash must fit in the c
 //   base: the floating base's 6x6 block, its Cholesky solve (aba_factor.cuh:90-108,138-155);
 //   F2 (root->leaf): qdd per hinge body (aba_factor.cuh:156-164).
 // bias_out (optional, per world slot, global memory) receives qfrc_bias.
-__device__ void group_smooth(float* grp, const G1Tables& T, int lane, const float* const* bdt_w, float* const* bias_out,
-                             const float* bdt_all = nullptr) {
+__device__ void group_detect(float* grp, const G1Tables& T, int lane);
+__device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float* const* bdt_w, float* const* bias_out,
+                            const float* bdt_all = nullptr, int allow_defer = 0) {
     const int w = lane >> 2, cl = lane & 3;
     const float* bdt = nullptr;  // world w's entry, by unrolled select (no run-time index)
     if (bdt_all) {
@@ -270,7 +270,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
     const bool on = w < GW && cl < T.nchain;
     float* fr = grp + (w < GW ? w : 0) * WFLOATS;
     const float *qp = fr + WL::QP, *qv = fr + WL::QV, *tau = fr + WL::TAU;
-    float *S = fr + WL::S, *BQ = fr + WL::BQ, *FOWN = fr + WL::FOWN, *UB = fr + WL::UB;
+    float *S = fr + WL::S, *BQ = fr + WL::BQ, *FOWN = fr + WL::FOWN;
     float *FU = fr + WL::FU, *FINVD = fr + WL::FINVD, *qacc = fr + WL::QACC, *XS = fr + WL::XS;
     float* bias = (bias_out && w < GW) ? bias_out[w] : nullptr;
     float* QS = grp + GW * WFLOATS;  // the group's contact workspace, idle until the contact solve
@@ -399,6 +399,15 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
     }
     __syncwarp();
     PROF_MARK(P_F1);
+    // contact detection needs only F1's kept frames.  With contacts in the group (and
+    // allow_defer), the base solve and F2 are left to the contact solve's back-solve step
+    // (lane_solve, four more lanes), off the path to the contact batch.
+    group_detect(grp, T, lane);
+    PROF_MARK(P_DETECT);
+    int anycon = 0;
+#pragma unroll
+    for (int ww = 0; ww < GW; ++ww) anycon |= reinterpret_cast<const int*>(grp + ww * WFLOATS + WL::MISC)[0];
+    const bool defer = allow_defer && anycon != 0;
 
     // ---- B1: leaf -> root along the chains.  The contribution of the previous (child) body
     // of the chain is carried in registers; other children (chain heads below a branch body)
@@ -468,7 +477,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                     u2[0] = make_float2(U[0], U[1]); u2[1] = make_float2(U[2], U[3]); u2[2] = make_float2(U[4], U[5]);
                 }
                 FINVD[b] = invD;
-                UB[b] = u;
+                qacc[d] = u;  // u_b parks in qacc[d] until the root -> leaf pass
 #pragma unroll
                 for (int r = 0; r < 6; ++r)
 #pragma unroll
@@ -558,6 +567,10 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
             }
 #pragma unroll
         for (int k = 0; k < 36; ++k) L6[k] = Dm[k];
+      if (defer) {  // the base solve and the root -> leaf pass run later, in lane_solve
+#pragma unroll
+        for (int k = 0; k < 6; ++k) qacc[k] = q6[k];
+      } else {
 #pragma unroll
         for (int i = 0; i < 6; ++i) {
             float acc = q6[i];
@@ -582,9 +595,11 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
             for (int k = 0; k < 6; ++k) acc += S[6 * k + i] * q6[k];
             A1[i] = acc;
         }
+      }
     }
     __syncwarp();
     PROF_MARK(P_BASE);
+    if (defer) return 1;
 
     // ---- F2: root -> leaf, qdd per hinge body
     {
@@ -606,7 +621,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
                 float s2 = 0.f;
                 s2 += u01.x * a[0]; s2 += u01.y * a[1]; s2 += u23.x * a[2];
                 s2 += u23.y * a[3]; s2 += u45.x * a[4]; s2 += u45.y * a[5];
-                const float qdd = (UB[b] - s2) * FINVD[b];
+                const float qdd = (qacc[d] - s2) * FINVD[b];
                 qacc[d] = qdd;
                 const float2* S2 = reinterpret_cast<const float2*>(S + 6 * d);
                 const float2 s01 = S2[0], s23 = S2[1], s45 = S2[2];
@@ -622,6 +637,7 @@ __device__ void group_smooth(float* grp, const G1Tables& T, int lane, const floa
         }
     }
     PROF_MARK(P_F2);
+    return 0;
 }
 
 // ------------------------------------------------------------------ M^-1 apply, one lane
@@ -874,8 +890,11 @@ struct Batch {
 // by side; the Delassus matrix is block diagonal over worlds and each world's PGS sweeps
 // its own rows in order, all worlds in the same pass.  f -> cw[FF] (world x's rows start at
 // 4*coff[x]).
+// smooth_lanes: lanes 32 - GW .. 31 also finish the deferred smooth solves of the group's
+// worlds (qacc_smooth = (M + dtB)^-1 (tau - bias) from the u_b parked in QACC), in the same
+// lane_solve step as the contact-basis columns (at most 24).
 __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables& T, int lane, int pgs_iters, float mu,
-                                          const Batch B) {
+                                          const Batch B, int smooth_lanes) {
     float* MM = cw + CL::MM;
     float* EB = cw + CL::EB;
     const int nc = B.cof(B.nw), nb = 3 * nc, nefc_all = 4 * nc;
@@ -900,11 +919,26 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
     }
     __syncwarp();
     PROF_MARK(P_CSETUP);
-    if (lane < nb) {
-        const int gc = lane / 3, x = B.world_of(gc);
-        const float* fr = grp + B.wof(x) * WFLOATS;
-        const int s = reinterpret_cast<const int*>(fr + WL::CON)[gc - B.cof(x)];
-        lane_solve(fr, T, MM + lane * MSTR, cw + CL::GRAM + lane * SOLVE_SCRATCH, T.foot_chains[s]);
+    static_assert(3 * MAXCON <= 32 - GW, "contact-basis columns and smooth lanes share the warp");
+    const bool sm = smooth_lanes && lane >= 32 - GW;
+    if (lane < nb || sm) {
+        float* fr;
+        float *xy, *scr;
+        int chains;
+        if (sm) {  // world slot lane - (32 - GW): rhs = u_b in QACC, no leaf -> root pass
+            fr = grp + (lane - (32 - GW)) * WFLOATS;
+            xy = fr + WL::QACC;
+            scr = fr + WL::HB;  // B1's hand-off area, dead after the base block
+            chains = 0;
+        } else {
+            const int gc = lane / 3, x = B.world_of(gc);
+            fr = grp + B.wof(x) * WFLOATS;
+            const int s = reinterpret_cast<const int*>(fr + WL::CON)[gc - B.cof(x)];
+            xy = MM + lane * MSTR;
+            scr = cw + CL::GRAM + lane * SOLVE_SCRATCH;
+            chains = T.foot_chains[s];
+        }
+        lane_solve(fr, T, xy, scr, chains);
     }
     __syncwarp();
     PROF_MARK(P_SOLVE);
@@ -1068,19 +1102,18 @@ __device__ __noinline__ void batch_contact(float* grp, float* cw, const G1Tables
 }
 
 // Smooth dynamics and contact detection for the GW worlds of the warp; ncon per world.
-__device__ void group_smooth_detect(float* grp, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
-                                    int* ncon, float* const* qs_out = nullptr) {
-    group_smooth(grp, T, lane, opt.bdt, bias_out, opt.bdt_all);
-    PROF_BEGIN();
+// returns 1 when the base solve and F2 were deferred to the contact solve (allow_defer)
+__device__ int group_smooth_detect(float* grp, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
+                                   int* ncon, float* const* qs_out = nullptr, int allow_defer = 0) {
+    const int defer = group_smooth(grp, T, lane, opt.bdt, bias_out, opt.bdt_all, allow_defer && !qs_out);
     if (qs_out)
         for (int it = lane; it < GW * NV; it += 32) {
             const int w = it / NV, d = it % NV;
             if (qs_out[w]) qs_out[w][d] = grp[w * WFLOATS + WL::QACC + d];
         }
-    group_detect(grp, T, lane);
-    PROF_MARK(P_DETECT);
 #pragma unroll
     for (int w = 0; w < GW; ++w) ncon[w] = reinterpret_cast<const int*>(grp + w * WFLOATS + WL::MISC)[0];
+    return defer;
 }
 
 // Full per-substep generalised acceleration for the GW worlds of the warp (qp, qv, tau
@@ -1090,9 +1123,9 @@ __device__ void group_smooth_detect(float* grp, const G1Tables& T, int lane, con
 // barrier 1 after the smooth dynamics, bit 1 -- after the contact solve.
 __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, const QaccOpts& opt, float* const* bias_out,
                            float* const* f_out, int* ncon_out, float* const* qs_out = nullptr, int midbar = 0,
-                           int bar_threads = 0) {
+                           int bar_threads = 0, int allow_defer = 0) {
     int ncon[GW];
-    group_smooth_detect(grp, T, lane, opt, bias_out, ncon, qs_out);
+    int smooth_lanes = group_smooth_detect(grp, T, lane, opt, bias_out, ncon, qs_out, allow_defer);
     if (midbar & 1) asm volatile("bar.sync 1, %0;" ::"r"(bar_threads) : "memory");
 #pragma unroll
     for (int w = 0; w < GW; ++w) {
@@ -1105,7 +1138,8 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
 #ifdef G1_PROF
         if (lane == 0) atomicAdd(&g_prof[47 + B.cof(B.nw)], 1ull);  // batches by contact count 1..8
 #endif
-        batch_contact(grp, cw, T, lane, opt.pgs_iters, opt.mu, B);
+        batch_contact(grp, cw, T, lane, opt.pgs_iters, opt.mu, B, smooth_lanes);
+        smooth_lanes = 0;  // the first batch finished the deferred smooth solves
         if (f_out)
 #pragma unroll
             for (int x = 0; x < GW; ++x)

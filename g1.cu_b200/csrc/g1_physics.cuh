@@ -248,14 +248,21 @@ static_assert(4 * GW * NB <= CL::SIZE, "F1's orientation stash must fit in the c
 // Lane 4w + l walks chain l of world w with the running body state in registers; hand-offs
 // through shared memory only at branch bodies.  Sweeps:
 //   F1 (root->leaf): FK (dynamics.cuh:47-88), S (aba_bias.cuh:380-398), RNE partial
-//      velocities / cdof_dot / accelerations (aba_bias.cuh:419-457), body forces (:458-466);
+//      velocities / cdof_dot / accelerations (aba_bias.cuh:419-457); then a second pass, one
+//      lane per (world, body), for the body forces (:458-466) and kept world inertias;
+//   contact detection (group_detect: it needs only F1's kept body frames);
 //   B1 (leaf->root): subtree forces -> bias (aba_bias.cuh:467-475), the articulated-inertia
 //      factor (aba_factor.cuh:76-88) and, fused, the bias-force pass of the smooth solve
 //      (aba_factor.cuh:128-136).  A body adds its children's contributions in descending
 //      child index -- the order in which the reference's b-descending loops push them;
 //   base: the floating base's 6x6 block, its Cholesky solve (aba_factor.cuh:90-108,138-155);
 //   F2 (root->leaf): qdd per hinge body (aba_factor.cuh:156-164).
-// bias_out (optional, per world slot, global memory) receives qfrc_bias.
+// B1 parks u_b in qacc[d]; the base solve and F2 turn it into qacc_smooth.  With allow_defer
+// and a contact in the group, those two steps are skipped here (the base block leaves its
+// right-hand side in qacc[0..5]) and the function returns 1: batch_contact finishes them in
+// its lane_solve step.  Otherwise it returns 0 with qacc_smooth in QACC.
+// bias_out (optional, per world slot, global memory) receives qfrc_bias.  bdt_all, when
+// non-null, is the dt*B diagonal of every world slot (else bdt_w per slot).
 __device__ void group_detect(float* grp, const G1Tables& T, int lane);
 __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float* const* bdt_w, float* const* bias_out,
                             const float* bdt_all = nullptr, int allow_defer = 0) {

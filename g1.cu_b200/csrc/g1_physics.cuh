@@ -436,6 +436,14 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 }
 #pragma unroll
                 for (int i = 0; i < 6; ++i) pa[i] = 0.f;
+                if (T.branch_slot[b] < 0) {  // one child -- the walk's previous body -- or a leaf
+                    if (k > 0) {
+#pragma unroll
+                        for (int i = 0; i < 21; ++i) ia[i] += cia[i];
+#pragma unroll
+                        for (int i = 0; i < 6; ++i) { f[i] += cf[i]; pa[i] += cpa[i]; }
+                    }
+                } else
                 for (int q = T.child_start[b]; q < T.child_start[b + 1]; ++q) {
                     const int c = T.child_list[q];
                     if (c == carried) {

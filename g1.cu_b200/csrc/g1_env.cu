@@ -1065,6 +1065,8 @@ static int upload_tables(int dev) {
         if (cudaFuncSetAttribute(k_g1, cudaFuncAttributeMaxDynamicSharedMemorySize, p.total_bytes) != cudaSuccess) rc = -2;
         if (cudaFuncSetAttribute(k_qacc, cudaFuncAttributeMaxDynamicSharedMemorySize, p.total_bytes) != cudaSuccess) rc = -3;
         if (T.nchain > CPW) rc = -4;  // the chain-lane mapping holds at most CPW chains
+        for (int c = 0; c < T.nchain; ++c)
+            if (T.chain_len[c] > G1_MAXCLEN) rc = -5;  // the per-step table holds G1_MAXCLEN bodies
     });
     return rc;
 }

@@ -346,7 +346,8 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
         for (int s = 0; s < T.nsteps; ++s) {
             const int k = on ? s - T.chain_start[cl] : -1;
             if (k >= 0 && k < T.chain_len[cl]) {
-                const int b = T.chain_body[cl][k];
+                const int4 cs = T.cstep[cl][k];
+                const int b = cs.x;
                 if (k == 0) {
                     const int par = T.parent[b];
                     if (par == 1) {
@@ -356,14 +357,14 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                         pos = ld3(st); quat = ld4(st + 3); wv = ld3(st + 7); vv = ld3(st + 10); aw = ld3(st + 13); av = ld3(st + 16);
                     }
                 }
-                const int j = T.body_jnt[b], d = T.dofadr[b];
+                const int j = cs.y, d = cs.w;
                 pos = add3(pos, qrot(quat, ld3(T.body_pos + 3 * b)));
                 quat = qmul(quat, ld4(T.body_quat + 4 * b));
                 const V3 an = ld3(T.jnt_pos + 3 * j), ax = ld3(T.jnt_axis + 3 * j);
                 const V3 anchor = add3(pos, qrot(quat, an));
-                float sn, cs;
-                sincosf(0.5f * qp[T.jnt_qposadr[j]], &sn, &cs);
-                quat = qmul(quat, Q4{cs, ax.x * sn, ax.y * sn, ax.z * sn});
+                float sn, csn;
+                sincosf(0.5f * qp[cs.z], &sn, &csn);
+                quat = qmul(quat, Q4{csn, ax.x * sn, ax.y * sn, ax.z * sn});
                 pos = sub3(anchor, qrot(quat, an));
                 if (T.xslot[b] >= 0) {
                     float* xs = XS + 8 * T.xslot[b];
@@ -426,7 +427,8 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
             const int len = on ? T.chain_len[cl] : 0;
             const int k = on ? s - T.chain_bstart[cl] : -1;
             if (k >= 0 && k < len) {
-                const int b = T.chain_body[cl][len - 1 - k], d = T.dofadr[b];
+                const int4 cs = T.cstep[cl][len - 1 - k];
+                const int b = cs.x, d = cs.w;
                 float ia[21], f[6], pa[6];
                 body_ia_kept(T, b, BQ + 9 * b, ia);
                 {
@@ -622,9 +624,9 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
         for (int s = 0; s < T.nsteps; ++s) {
             const int k = on ? s - T.chain_start[cl] : -1;
             if (k >= 0 && k < T.chain_len[cl]) {
-                const int b = T.chain_body[cl][k];
+                const int4 cs = T.cstep[cl][k];
+                const int b = cs.x, d = cs.w;
                 const int4 bi = T.binfo[b];
-                const int d = bi.x;
                 if (k == 0) {
                     const int par = bi.z;
                     const float* src = par == 1 ? fr + WL::A1 : fr + WL::HA + 8 * T.binfo[par].y;

@@ -31,6 +31,7 @@
 #define G1_NRHS (1 + 3 * G1_MAXCON)
 #define G1_MAXCHAIN 6
 #define G1_MAXBRANCH 2
+#define G1_MAXCLEN 12  // bodies per chain (the G1's longest chain, waist + left arm, has 10)
 #define G1_MAXXSLOT 4
 
 struct alignas(16) G1Tables {
@@ -66,6 +67,9 @@ struct alignas(16) G1Tables {
     int chain_len[G1_MAXCHAIN], chain_start[G1_MAXCHAIN];
     int chain_bstart[G1_MAXCHAIN];  // leaf->root sweep: step at which the chain's leaf is processed
     int chain_body[G1_MAXCHAIN][G1_NB];
+    // step k of chain c as one 16-byte load: {body, its joint, the joint's qpos address, the
+    // body's dof} -- a sweep step needs no dependent index loads after it
+    int4 cstep[G1_MAXCHAIN][G1_MAXCLEN];
     int branch_slot[G1_NB];  // bodies other than the base with >1 child: hand-off slot, else -1
     int head_chain[G1_NB];   // chain whose head is this body, else -1
     int xslot[G1_NB];        // pelvis and foot bodies: slot of their kept frame, else -1
@@ -236,6 +240,11 @@ static inline void g1_build_tables(G1Tables* T) {
         T->foot_chains[s] = mask;
     }
     for (int b = 0; b < G1_NB; ++b) T->binfo[b] = make_int4(T->dofadr[b], T->branch_slot[b], T->parent[b], 0);
+    for (int c = 0; c < T->nchain; ++c)
+        for (int k = 0; k < T->chain_len[c] && k < G1_MAXCLEN; ++k) {
+            const int bb = T->chain_body[c][k], j = T->body_jnt[bb];
+            T->cstep[c][k] = make_int4(bb, j, T->jnt_qposadr[j], T->dofadr[bb]);
+        }
     T->free_jnt = 0;
     for (int j = G1_NJ - 1; j >= 0; --j)
         if (G1M_JNT_TYPE[j] == 0) T->free_jnt = j;

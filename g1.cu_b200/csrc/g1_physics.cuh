@@ -275,6 +275,11 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
         for (int k = 0; k < GW; ++k) bdt = (w == k) ? bdt_w[k] : bdt;
     }
     const bool on = w < GW && cl < T.nchain;
+    // this lane's chain bounds and the sweep lengths, in registers for all three sweeps (the
+    // frame stores inside the sweeps would otherwise make the compiler reload them each step)
+    const int c_start = on ? T.chain_start[cl] : 0, c_len = on ? T.chain_len[cl] : 0;
+    const int c_bstart = on ? T.chain_bstart[cl] : 0;
+    const int n_fwd = T.nsteps, n_back = T.nsteps_back;
     float* fr = grp + (w < GW ? w : 0) * WFLOATS;
     const float *qp = fr + WL::QP, *qv = fr + WL::QV, *tau = fr + WL::TAU;
     float *S = fr + WL::S, *BQ = fr + WL::BQ, *FOWN = fr + WL::FOWN;
@@ -343,9 +348,9 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     {
         V3 pos = p, wv = bw, vv = bv, aw = baw, av = bav;
         Q4 quat = q1;
-        for (int s = 0; s < T.nsteps; ++s) {
-            const int k = on ? s - T.chain_start[cl] : -1;
-            if (k >= 0 && k < T.chain_len[cl]) {
+        for (int s = 0; s < n_fwd; ++s) {
+            const int k = on ? s - c_start : -1;
+            if (k >= 0 && k < c_len) {
                 const int4 cs = T.cstep[cl][k];
                 const int b = cs.x;
                 if (k == 0) {
@@ -423,9 +428,9 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     {
         float cia[21], cf[6], cpa[6];
         int carried = -1;
-        for (int s = 0; s < T.nsteps_back; ++s) {
-            const int len = on ? T.chain_len[cl] : 0;
-            const int k = on ? s - T.chain_bstart[cl] : -1;
+        for (int s = 0; s < n_back; ++s) {
+            const int len = c_len;
+            const int k = on ? s - c_bstart : -1;
             if (k >= 0 && k < len) {
                 const int4 cs = T.cstep[cl][len - 1 - k];
                 const int b = cs.x, d = cs.w;
@@ -621,9 +626,9 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     // ---- F2: root -> leaf, qdd per hinge body
     {
         float a[6];
-        for (int s = 0; s < T.nsteps; ++s) {
-            const int k = on ? s - T.chain_start[cl] : -1;
-            if (k >= 0 && k < T.chain_len[cl]) {
+        for (int s = 0; s < n_fwd; ++s) {
+            const int k = on ? s - c_start : -1;
+            if (k >= 0 && k < c_len) {
                 const int4 cs = T.cstep[cl][k];
                 const int b = cs.x, d = cs.w;
                 const int4 bi = T.binfo[b];

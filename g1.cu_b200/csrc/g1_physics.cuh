@@ -348,10 +348,12 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     {
         V3 pos = p, wv = bw, vv = bv, aw = baw, av = bav;
         Q4 quat = q1;
+        int4 cs_nx = T.cstep[cl & 3][0];  // the next step's entry, loaded one step ahead
         for (int s = 0; s < n_fwd; ++s) {
             const int k = on ? s - c_start : -1;
             if (k >= 0 && k < c_len) {
-                const int4 cs = T.cstep[cl][k];
+                const int4 cs = cs_nx;
+                cs_nx = T.cstep[cl][min(k + 1, G1_MAXCLEN - 1)];
                 const int b = cs.x;
                 if (k == 0) {
                     const int par = T.parent[b];
@@ -428,11 +430,13 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     {
         float cia[21], cf[6], cpa[6];
         int carried = -1;
+        int4 cs_nx = T.cstep[cl & 3][max(c_len - 1, 0)];  // the next step's entry, one step ahead
         for (int s = 0; s < n_back; ++s) {
             const int len = c_len;
             const int k = on ? s - c_bstart : -1;
             if (k >= 0 && k < len) {
-                const int4 cs = T.cstep[cl][len - 1 - k];
+                const int4 cs = cs_nx;
+                cs_nx = T.cstep[cl][max(len - 2 - k, 0)];
                 const int b = cs.x, d = cs.w;
                 float ia[21], f[6], pa[6];
                 body_ia_kept(T, b, BQ + 9 * b, ia);
@@ -626,10 +630,12 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     // ---- F2: root -> leaf, qdd per hinge body
     {
         float a[6];
+        int4 cs_nx = T.cstep[cl & 3][0];  // the next step's entry, loaded one step ahead
         for (int s = 0; s < n_fwd; ++s) {
             const int k = on ? s - c_start : -1;
             if (k >= 0 && k < c_len) {
-                const int4 cs = T.cstep[cl][k];
+                const int4 cs = cs_nx;
+                cs_nx = T.cstep[cl][min(k + 1, G1_MAXCLEN - 1)];
                 const int b = cs.x, d = cs.w;
                 const int4 bi = T.binfo[b];
                 if (k == 0) {

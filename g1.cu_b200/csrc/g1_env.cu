@@ -301,8 +301,9 @@ __device__ __noinline__ void policy_phase(const Params& P, const G1Tables& T, fl
         }
         // observations: raw to O, normalised straight into the three bf16 parts of A (8
         // inputs per thread; inputs 100..111 zero)
+        // consecutive threads take consecutive worlds (contiguous stores into A; see tf_layer)
         for (int e = threadIdx.x; e < nbw * 14; e += NTHREADS) {
-            const int w = e / 14, k0 = (e % 14) * 8, gw = wbeg + w;
+            const int w = e % nbw, k0 = (e / nbw) * 8, gw = wbeg + w;
             const float* qp = P.qp + (size_t)gw * NQ;
             const float* qv = P.qv + (size_t)gw * NV;
             const float* pa = P.pa + (size_t)gw * NU;

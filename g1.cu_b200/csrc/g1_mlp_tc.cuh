@@ -254,6 +254,7 @@ constexpr int dense_tc_smem() {
 using ::g1::g_prof;
 using ::g1::P_TF_MMA;
 using ::g1::P_TF_EPI;
+using ::g1::P_TF_EPI1;
 #endif
 constexpr int TF_ROWS = 64;
 constexpr int TF_KMAX = 256;
@@ -490,9 +491,14 @@ __device__ void tf_layer(TfShared* S, uint8_t* A, uint8_t* stages, const TfLayer
     }
     if (act >= 0) {
         __syncthreads();
+#ifdef G1_PROF
+        PROF_MARK(P_TF_EPI1);
+#endif
         const int ng = N / 8;
+        // consecutive threads take consecutive rows: their 16-byte stores into A are then
+        // contiguous (a row's column groups are 1024 bytes apart, one bank group)
         for (int e = tid; e < nrows * ng; e += NT) {
-            const int row = e / ng, c0 = (e % ng) * 8;
+            const int row = e % nrows, c0 = (e / nrows) * 8;
             const float4* src = reinterpret_cast<const float4*>(stg + row * sld + c0);
             const float4 a = src[0], b = src[1];
             float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};

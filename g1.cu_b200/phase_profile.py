@@ -21,7 +21,8 @@ LIB = os.path.join(HERE, "libg1env_prof.so")
 NAMES = ["policy", "F1", "B1", "base", "F2", "contact_setup", "back_solves", "gram", "pgs", "dq", "pd_torque",
          "end_of_step_wait", "integrate", "detect", "mlp_layer0", "sampling", "mlp_layer1", "mlp_head",
          "substep_barrier_wait", "energy", "mlp_mma_wait", "mlp_epilogue", "step_state_load", "reward_done",
-         "state_store_reset", "contact_sort", "kernel_total", "solve_leaf_to_root", "solve_base", "solve_root_to_leaf", "mlp_epilogue_stage"]
+         "state_store_reset", "contact_sort", "kernel_total", "solve_leaf_to_root", "solve_base", "solve_root_to_leaf", "mlp_epilogue_stage",
+         "mlp_epilogue_act"]
 
 
 def build():
@@ -60,7 +61,7 @@ def main():
     per["unattributed"] = per["kernel_total"] - sum(v for k, v in per.items()
                                                     if k not in ("kernel_total", "mlp_layer0", "mlp_layer1", "mlp_head",
                                                                  "sampling", "mlp_mma_wait", "mlp_epilogue",
-                                                                 "mlp_epilogue_stage", "solve_leaf_to_root", "solve_base", "solve_root_to_leaf"))
+                                                                 "mlp_epilogue_stage", "mlp_epilogue_act", "solve_leaf_to_root", "solve_base", "solve_root_to_leaf"))
     batches = [round(out[47 + c] / H / (nw_live // 7), 2) for c in range(1, 9)]
     print(json.dumps({"N": N, "H": H, "cycles_per_warp_per_control_step": per,
                       "contact_batches_per_cta_per_control_step_by_size_1_to_8": batches}))

@@ -356,7 +356,7 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 cs_nx = T.cstep[cl][min(k + 1, G1_MAXCLEN - 1)];
                 const int b = cs.x;
                 if (k == 0) {
-                    const int par = T.parent[b];
+                    const int par = cstep_parent(cs.y);
                     if (par == 1) {
                         pos = p; quat = q1; wv = bw; vv = bv; aw = baw; av = bav;
                     } else {
@@ -364,7 +364,8 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                         pos = ld3(st); quat = ld4(st + 3); wv = ld3(st + 7); vv = ld3(st + 10); aw = ld3(st + 13); av = ld3(st + 16);
                     }
                 }
-                const int j = cs.y, d = cs.w;
+                const int j = cstep_jnt(cs.y), d = cs.w;
+                const int xsl = cstep_xslot(cs.y), bsl = cstep_bslot(cs.y);
                 pos = add3(pos, qrot(quat, ld3(T.body_pos + 3 * b)));
                 quat = qmul(quat, ld4(T.body_quat + 4 * b));
                 const V3 an = ld3(T.jnt_pos + 3 * j), ax = ld3(T.jnt_axis + 3 * j);
@@ -373,8 +374,8 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 sincosf(0.5f * qp[cs.z], &sn, &csn);
                 quat = qmul(quat, Q4{csn, ax.x * sn, ax.y * sn, ax.z * sn});
                 pos = sub3(anchor, qrot(quat, an));
-                if (T.xslot[b] >= 0) {
-                    float* xs = XS + 8 * T.xslot[b];
+                if (xsl >= 0) {
+                    float* xs = XS + 8 * xsl;
                     st4(xs, quat); st3(xs + 4, pos);
                 }
                 const V3 sw = qrot(quat, ax);
@@ -387,8 +388,8 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 aw = {aw.x + sdw.x * qd, aw.y + sdw.y * qd, aw.z + sdw.z * qd};
                 av = {av.x + sdv.x * qd, av.y + sdv.y * qd, av.z + sdv.z * qd};
                 stash_body(QS + 4 * (w * NB + b), quat, pos, wv, vv, aw, av, FOWN + 6 * b, BQ + 9 * b);
-                if (T.branch_slot[b] >= 0) {
-                    float* st = fr + WL::HF + 20 * T.branch_slot[b];
+                if (bsl >= 0) {
+                    float* st = fr + WL::HF + 20 * bsl;
                     st3(st, pos); st4(st + 3, quat); st3(st + 7, wv); st3(st + 10, vv); st3(st + 13, aw); st3(st + 16, av);
                 }
             }
@@ -447,7 +448,7 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 }
 #pragma unroll
                 for (int i = 0; i < 6; ++i) pa[i] = 0.f;
-                if (T.branch_slot[b] < 0) {  // one child -- the walk's previous body -- or a leaf
+                if (cstep_bslot(cs.y) < 0) {  // one child -- the walk's previous body -- or a leaf
                     if (k > 0) {
 #pragma unroll
                         for (int i = 0; i < 21; ++i) ia[i] += cia[i];
@@ -637,9 +638,9 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 const int4 cs = cs_nx;
                 cs_nx = T.cstep[cl][min(k + 1, G1_MAXCLEN - 1)];
                 const int b = cs.x, d = cs.w;
-                const int4 bi = T.binfo[b];
+                const int bsl = cstep_bslot(cs.y);
                 if (k == 0) {
-                    const int par = bi.z;
+                    const int par = cstep_parent(cs.y);
                     const float* src = par == 1 ? fr + WL::A1 : fr + WL::HA + 8 * T.binfo[par].y;
 #pragma unroll
                     for (int i = 0; i < 6; ++i) a[i] = src[i];
@@ -655,8 +656,8 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 const float2 s01 = S2[0], s23 = S2[1], s45 = S2[2];
                 a[0] = a[0] + s01.x * qdd; a[1] = a[1] + s01.y * qdd; a[2] = a[2] + s23.x * qdd;
                 a[3] = a[3] + s23.y * qdd; a[4] = a[4] + s45.x * qdd; a[5] = a[5] + s45.y * qdd;
-                if (bi.y >= 0) {
-                    float* st = fr + WL::HA + 8 * bi.y;
+                if (bsl >= 0) {
+                    float* st = fr + WL::HA + 8 * bsl;
 #pragma unroll
                     for (int i = 0; i < 6; ++i) st[i] = a[i];
                 }

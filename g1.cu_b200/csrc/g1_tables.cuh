@@ -34,6 +34,17 @@
 #define G1_MAXCLEN 12  // bodies per chain (the G1's longest chain, waist + left arm, has 10)
 #define G1_MAXXSLOT 4
 
+// cstep's packed field: joint (bits 0-7), branch slot + 1 (8-11), kept-frame slot + 1
+// (12-15), parent body (16-23)
+__host__ __device__ constexpr int cstep_pack(int jnt, int bslot, int xslot, int parent) {
+    return jnt | ((bslot + 1) << 8) | ((xslot + 1) << 12) | (parent << 16);
+}
+__host__ __device__ __forceinline__ int cstep_jnt(int y) { return y & 0xFF; }
+__host__ __device__ __forceinline__ int cstep_bslot(int y) { return ((y >> 8) & 0xF) - 1; }
+__host__ __device__ __forceinline__ int cstep_xslot(int y) { return ((y >> 12) & 0xF) - 1; }
+__host__ __device__ __forceinline__ int cstep_parent(int y) { return (y >> 16) & 0xFF; }
+static_assert(G1_NJ <= 256 && G1_MAXBRANCH < 15 && G1_MAXXSLOT < 15 && G1_NB <= 256, "cstep packing");
+
 struct alignas(16) G1Tables {
     float body_pos[G1_NB * 3], body_quat[G1_NB * 4], body_ipos[G1_NB * 3], body_iquat[G1_NB * 4];
     float body_mass[G1_NB], body_inertia[G1_NB * 3];
@@ -67,8 +78,9 @@ struct alignas(16) G1Tables {
     int chain_len[G1_MAXCHAIN], chain_start[G1_MAXCHAIN];
     int chain_bstart[G1_MAXCHAIN];  // leaf->root sweep: step at which the chain's leaf is processed
     int chain_body[G1_MAXCHAIN][G1_NB];
-    // step k of chain c as one 16-byte load: {body, its joint, the joint's qpos address, the
-    // body's dof} -- a sweep step needs no dependent index loads after it
+    // step k of chain c as one 16-byte load: {body, packed (joint, branch slot, kept-frame
+    // slot, parent) -- cstep_pack --, the joint's qpos address, the body's dof}: a sweep step
+    // needs no dependent index loads after it
     int4 cstep[G1_MAXCHAIN][G1_MAXCLEN];
     int branch_slot[G1_NB];  // bodies other than the base with >1 child: hand-off slot, else -1
     int head_chain[G1_NB];   // chain whose head is this body, else -1
@@ -243,7 +255,8 @@ static inline void g1_build_tables(G1Tables* T) {
     for (int c = 0; c < T->nchain; ++c)
         for (int k = 0; k < T->chain_len[c] && k < G1_MAXCLEN; ++k) {
             const int bb = T->chain_body[c][k], j = T->body_jnt[bb];
-            T->cstep[c][k] = make_int4(bb, j, T->jnt_qposadr[j], T->dofadr[bb]);
+            T->cstep[c][k] = make_int4(bb, cstep_pack(j, T->branch_slot[bb], T->xslot[bb], T->parent[bb]),
+                                       T->jnt_qposadr[j], T->dofadr[bb]);
         }
     T->free_jnt = 0;
     for (int j = G1_NJ - 1; j >= 0; --j)

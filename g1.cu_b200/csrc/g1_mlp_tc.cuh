@@ -255,6 +255,7 @@ using ::g1::g_prof;
 using ::g1::P_TF_MMA;
 using ::g1::P_TF_EPI;
 using ::g1::P_TF_EPI1;
+using ::g1::P_TF_EPI2;
 #endif
 constexpr int TF_ROWS = 64;
 constexpr int TF_KMAX = 256;
@@ -509,6 +510,9 @@ __device__ void tf_layer(TfShared* S, uint8_t* A, uint8_t* stages, const TfLayer
             }
             tf_store8(A, row, c0, v);
         }
+#ifdef G1_PROF
+        PROF_MARK(P_TF_EPI2);
+#endif
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;");

@@ -451,8 +451,8 @@ def main():
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": 2 * args.steps,
                 "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
-                             "frac": achieved / fp32_peak, "traffic": 73.1e6,
-                             "traffic_source": "ncu dram__bytes_read+write of one H=2 launch (4.57 MB), scaled x16 to H=32 (profiles/k_g1_rollout_n8192_h32.md)",
+                             "frac": achieved / fp32_peak, "traffic": 72.5e6,
+                             "traffic_source": "ncu dram__bytes_read+write of one H=2 launch (4.53 MB), scaled x16 to H=32 (profiles/k_g1_rollout_n8192_h32.md)",
                              "peak_source": f"nominal FP32 FMA rate: {sm_count} SMs x 128 lanes x 2 x {clk:.0f} MHz; the policy "
                                             f"MLP (counted at its algorithmic fp32 FLOPs) runs on the tensor cores "
                                             f"(MEASURED_PEAKS.json has no FP32 figure; its hbm/bf16 peaks are {peak_src})",

@@ -8,10 +8,11 @@
 //   * one persistent kernel per call; a CTA owns a contiguous block of worlds for the whole
 //     horizon (a CTA per SM: the grid is sized to the SM count);
 //   * per control step the CTA first runs the POLICY phase over its whole world block --
-//     observations, normalisation, the actor-critic MLP as a dense contraction staged in
-//     shared memory, Philox Gaussian sampling, trajectory writes -- then the PHYSICS phase,
-//     where each warp takes one world at a time from the block (shared-memory queue) and
-//     advances it S substeps with its frame in shared memory (g1_physics.cuh);
+//     observations, normalisation, the actor-critic MLP (tcgen05 split-bf16 or FFMA),
+//     Philox Gaussian sampling, trajectory writes -- then the PHYSICS phase: the block's
+//     worlds are sorted by their last contact count and dealt in snake order into groups of
+//     4, one group per warp, and each warp advances its group S substeps with the worlds'
+//     frames in shared memory (g1_physics.cuh);
 //   * world state (qpos, qvel, previous action, episode step) stays in HBM/L2 between
 //     control steps ([N,36], [N,35], [N,29], [N] like the reference's EnvState).
 // Errors: C-ABI functions keep the reference's void returns; failures are recorded and
@@ -45,6 +46,16 @@ using namespace g1;
 #define MAX_WB 64          // worlds per CTA block, upper bound (MLP activations in smem)
 #define MAX_HIDDEN 4
 #define XSTR 104           // normalized-obs row stride (floats)
+// Barrier schedule of the physics phase, fixed at build time.  G1_LOCKSTEP > 0: the CTA's
+// warps meet at a named barrier every G1_LOCKSTEP substeps (they then run the same code, and
+// instruction fetch stays in cache).  G1_MIDBAR bit 1: a second barrier per substep, after
+// the contact solve (measured 0.8 % faster: the warps integrate on the same code too).
+#ifndef G1_LOCKSTEP
+#define G1_LOCKSTEP 1
+#endif
+#ifndef G1_MIDBAR
+#define G1_MIDBAR 2
+#endif
 
 __constant__ G1Tables c_tab;
 
@@ -1082,10 +1093,8 @@ static Params base_params(EnvState* E) {
     for (int i = 0; i < MAX_HIDDEN; ++i) P.hid[i] = E->hid[i];
     P.ncon_hist = E->ncon_hist;
     P.ncon_last = E->ncon_last;
-    P.lockstep = getenv("G1_LOCKSTEP") ? atoi(getenv("G1_LOCKSTEP")) : 1;
-    // a second barrier per substep, after the contact solve (measured 0.8 % faster: the warps
-    // then integrate and start the next substep on the same code)
-    P.midbar = getenv("G1_MIDBAR") ? atoi(getenv("G1_MIDBAR")) : 2;
+    P.lockstep = G1_LOCKSTEP;
+    P.midbar = G1_MIDBAR;
     // worlds per CTA: spread over all SMs, at most MAX_WB (then CTAs run in waves)
     int wb = (E->N + E->sm_count - 1) / E->sm_count;
     if (wb > 2 * GW * NWARPS) wb = 2 * GW * NWARPS;  // large N: blocks of two full rounds of groups
@@ -1334,6 +1343,22 @@ static int tc_error(EnvState* E) {
     return herr;
 }
 
+// Test entry (not part of the public header): runs k_wait_probe on the env's stream with a
+// spin limit of `spin_limit` iterations; the timed-out wait is reported through the same
+// device flag as the rollout's, read with g1_env_tc_status.  Returns the CUDA status.
+extern "C" int g1_env_test_wait_timeout(void* h, unsigned spin_limit) {
+    EnvState* E = (EnvState*)h;
+    if (!E->derr) {
+        CKR(cudaMalloc(&E->derr, sizeof(int)), -1);
+        CKR(cudaMemset(E->derr, 0, sizeof(int)), -1);
+    }
+    g1tc::k_wait_probe<<<1, 224, 0, E->stream>>>(E->derr, spin_limit);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(E->stream);
+    if (e != cudaSuccess) set_error((int)e, "g1_env_test_wait_timeout", cudaGetErrorString(e));
+    return (int)e;
+}
+
 // ------------------------------------------------------------------ allocation-free rollout
 // g1_rollout repacks the policy weights into a buffer the env allocates on first use (and
 // reallocates when the policy grows).  g1_rollout_noalloc keeps that repacked copy in this
@@ -1346,14 +1371,21 @@ static __device__ __align__(256) float g_noalloc_wt[G1_NOALLOC_WT_FLOATS];
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_ptr[64];  // device address of g_noalloc_wt, per device ordinal
 
-// Device address of the static weight area on the current device, looked up once per
-// device (cudaGetSymbolAddress; the host-side name g_noalloc_wt is not a device address).
+// Device address of the static weight area on device `dev`, looked up once per device
+// (cudaGetSymbolAddress; the host-side name g_noalloc_wt is not a device address).  The
+// symbol resolves on the CURRENT device, so the lookup makes `dev` current for its duration
+// and restores the caller's device afterwards.
 static float* noalloc_area(int dev) {
     if (dev < 0 || dev >= 64) { set_error(-22, "g1_rollout_noalloc", "device ordinal out of range"); return nullptr; }
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_ptr[dev]) {
+        int prev = -1;
+        CKR(cudaGetDevice(&prev), nullptr);
+        if (prev != dev) CKR(cudaSetDevice(dev), nullptr);
         float* ptr = nullptr;
-        CKR(cudaGetSymbolAddress((void**)&ptr, g_noalloc_wt), nullptr);
+        const cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_wt);
+        if (prev != dev) cudaSetDevice(prev);
+        if (e != cudaSuccess) { set_error((int)e, "g1_rollout_noalloc", cudaGetErrorString(e)); return nullptr; }
         g_noalloc_ptr[dev] = ptr;
     }
     return g_noalloc_ptr[dev];
@@ -1611,6 +1643,12 @@ void g1_rollout_noalloc(void* h, int H, const float* W, const float* mean, const
                         float* LP, float* V, float* R, float* D, float* Vlast) {
     EnvState* E = (EnvState*)h;
     if (H <= 0) return;
+    // only the in-kernel FFMA policy path reads its weights from this area: the bf16
+    // tensor-core policy (precision 1) and a separate value network keep env-owned buffers
+    if (E->prec == 1 || E->vnh > 0) {
+        set_error(-22, "g1_rollout_noalloc", "supports the fp32 in-kernel policy only (not precision 1, not a separate value network)");
+        return;
+    }
     const size_t need = policy_floats(E->nh, E->hid);
     if (need > (size_t)G1_NOALLOC_WT_FLOATS) {
         char msg[160];

@@ -46,8 +46,8 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
-    for (uint32_t it = 0; it < SPIN_LIMIT; ++it) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase, uint32_t limit = SPIN_LIMIT) {
+    for (uint32_t it = 0; it < limit; ++it) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -363,6 +363,20 @@ __device__ __forceinline__ void tf_release(TfShared* S) {
     asm volatile("tcgen05.fence::after_thread_sync;");
     if ((threadIdx.x >> 5) == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(S->st[0]), "r"(512));
+}
+
+// Failure-path check of the bounded waits (test entry g1_env_test_wait_timeout): sets up the
+// policy pipeline exactly as k_g1 does (barriers, 512 TMEM columns), then the MMA-issuing
+// thread waits on a stage's `full` barrier that nothing arrives at -- no bulk copy and no
+// MMA is in flight -- with a spin limit given at launch.  The wait runs out, the error flag
+// is set as in the rollout, and TMEM is released before the CTA exits.
+__global__ void __launch_bounds__(224, 1) k_wait_probe(int* err, uint32_t limit) {
+    __shared__ TfShared S;
+    tf_init(&S);
+    bool ok = true;
+    if (threadIdx.x == 64) ok = mbar_wait(smem_u32(&S.bars[0]), 0u, limit);
+    if (!ok) atomicExch(err, 2);
+    tf_release(&S);
 }
 
 // copy thread: bring chunk c of layer L in as global chunk g, once the stage's previous

@@ -58,7 +58,10 @@ void g1_rollout(void* h, int H, const float* W, const float* mean, const float* 
  * The repacked policy weights live in a fixed 512 KiB device area (131,072 floats) shared by
  * all calls and all envs on a device: policies needing more are rejected (last error set),
  * and calls that overlap on the GPU race on the area.  The first call on each device looks
- * up the area's address; make it before any stream capture.  Arguments as g1_rollout. */
+ * up the area's address; make it before any stream capture.  Arguments as g1_rollout.
+ * The policy always runs on the in-kernel FFMA contraction, so results equal g1_rollout's
+ * under precision 2 ("fp32-ffma") and differ slightly (rounding) from its default tensor-core
+ * MLP.  Envs set to precision 1 or given a separate value network are rejected. */
 void g1_rollout_noalloc(void* h, int H, const float* W, const float* mean, const float* var, float* O, float* A,
                         float* LP, float* V, float* R, float* D, float* Vlast);
 

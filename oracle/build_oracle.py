@@ -8,6 +8,8 @@ Outputs (all git-ignored, all travel with the repository snapshot to a GPU box):
   oracle/_ref/libg1ref_cuda.so                       -- reference physics, CUDA sm_100a harness
   oracle/_ref/libg1env_ref.so                        -- the reference's g1_env.cu as shipped,
                                                         compiled for sm_100a (its own C-ABI)
+  oracle/_ref/trainer/scripts/ppo.py, ppo_fused.py   -- the reference's trainer, staged
+                                                        unchanged for the drop-in test
 
 The reference pieces are compiled from the sources where they lie (-I<ref>/src); nothing is
 copied into this repository.
@@ -17,7 +19,7 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_DEFAULT = "/root/reference"
+REF_DEFAULT = os.environ.get("G1_REFERENCE_ROOT", "/root/reference")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -68,7 +70,22 @@ def build_ref(ref_root=None, force=False, cuda=True):
         env_src = os.path.join(src_dir, "g1_env.cu")
         if force or _stale(out, [env_src] + ref_srcs):
             _run(["nvcc"] + ARCH + ["-O3", "-Xcompiler", "-fPIC", "--shared", "-w", env_src, "-lcurand", "-o", out])
+    stage_ref_trainer(ref_root, out_dir)
     return out_dir
+
+
+def stage_ref_trainer(ref_root, out_dir):
+    """Stage the reference's own trainer scripts, byte for byte, into oracle/_ref/trainer/
+    (git-ignored, like the reference builds; it travels with the snapshot to a GPU box,
+    which has no reference tree).  The drop-in test runs them unmodified against this
+    repository's libg1env.so."""
+    import shutil
+    dst = os.path.join(out_dir, "trainer", "scripts")
+    os.makedirs(dst, exist_ok=True)
+    for f in ("ppo.py", "ppo_fused.py"):
+        src = os.path.join(ref_root, "scripts", f)
+        if os.path.exists(src) and _stale(os.path.join(dst, f), [src]):
+            shutil.copyfile(src, os.path.join(dst, f))
 
 
 if __name__ == "__main__":

@@ -100,7 +100,7 @@ def main(ref_root):
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    root = args[0] if args else "/root/reference"
+    root = args[0] if args else os.environ.get("G1_REFERENCE_ROOT", "/root/reference")
     if "--policy-only" in sys.argv:
         export_finish_policy(root)
     else:

@@ -64,7 +64,10 @@ def _worker(rank, world, port, q):
     out = ac(x[:8])[0].sum() * (rank + 1)
     out.backward()
     ppo_fused.allreduce_grads(list(ac.parameters()))
-    q.put((rank, x, norm.mean, norm.var, norm.count, adv, nadv, ac.mu.weight.grad.clone()))
+    # tensors travel as numpy arrays (pickled by value): a tensor would be passed as a shared
+    # memory handle, which breaks when this process exits before the parent unpickles it
+    q.put(tuple(t.detach().numpy().copy() if torch.is_tensor(t) else t
+                for t in (rank, x, norm.mean, norm.var, norm.count, adv, nadv, ac.mu.weight.grad)))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -77,6 +80,7 @@ def test_distributed_stats_match_single_process():
     for p in ps:
         p.start()
     res = sorted([q.get(timeout=120) for _ in range(world)], key=lambda r: r[0])
+    res = [tuple(torch.from_numpy(v) if hasattr(v, "dtype") and hasattr(v, "shape") else v for v in r) for r in res]
     for p in ps:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -74,6 +74,37 @@ def test_qacc_vs_reference_cuda_fp32(gpu_qacc, states):
     assert np.percentile(e, 99) <= 5e-6
 
 
+@pytest.mark.skipif(not os.path.exists(REF_CUDA), reason="reference CUDA build not present")
+def test_substep_qpos_qvel_vs_reference_cuda_fp32(g1, states):
+    """One full substep -- PD torque, env_qacc, velocity update and guard, integrate_pos
+    (src/g1_env.cu:123-161, dynamics.cuh:333-355) -- against the reference's own CUDA fp32
+    code on the same 4096 states and random actions: per-state relative L2 error of qpos and
+    of qvel max <= 1e-5.  Runs this repo's host-loop step with S = 1; worlds that the step
+    ends (fall: base height < 0.45 or uprightness < 0.5) are auto-reset and left out."""
+    qp, qv, _ = states
+    n = qp.shape[0]
+    rng = np.random.default_rng(17)
+    act = rng.uniform(-1, 1, (n, 29)).astype(np.float32)
+    L = ctypes.CDLL(REF_CUDA)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    d = [torch.tensor(x).cuda().contiguous() for x in (qp, qv, act)]
+    qp_ref, qv_ref = torch.zeros(n, 36, device="cuda"), torch.zeros(n, 35, device="cuda")
+    assert L.ref_cuda_substep(n, *[vp(t) for t in d], 8, vp(qp_ref), vp(qv_ref)) == 0
+    env = g1.G1Env(n, 1, 8, seed=3)
+    env.set_state(qp, qv, np.zeros((n, 29), np.float32), np.zeros(n, np.int32))
+    _, _, done = env.step(act)
+    gq, gv = env.get_state()[:2]
+    env.close()
+    keep = done == 0
+    assert keep.sum() >= 0.95 * n
+    eq = relrows(gq[keep], qp_ref.cpu().numpy()[keep])
+    ev = relrows(gv[keep], qv_ref.cpu().numpy()[keep])
+    print(f"one substep vs reference CUDA fp32 over {keep.sum()} states: qpos max {eq.max():.2e}, "
+          f"qvel max {ev.max():.2e} p99 {np.percentile(ev, 99):.2e}")
+    assert eq.max() <= 1e-5, eq.max()
+    assert ev.max() <= 1e-5, ev.max()
+
+
 def test_qacc_vs_fp64_and_fp32_oracle(gpu_qacc, oracle_qacc):
     o32, o64 = oracle_qacc
     assert (gpu_qacc["ncon"] == o64["ncon"]).all()
@@ -146,11 +177,14 @@ def _bufs(H, N):
 
 @pytest.mark.parametrize("N", [1, 37, 256])
 @pytest.mark.parametrize("act", ["tanh", "elu"])
-def test_rollout_vs_oracle(g1, N, act):
+@pytest.mark.parametrize("path", ["tensor-core", "fp32-ffma", "noalloc"])
+def test_rollout_vs_oracle(g1, N, act, path):
+    """The three fp32 policy paths against the oracle: the default tensor-core MLP, the FFMA
+    contraction (precision "fp32-ffma") and g1_rollout_noalloc (always FFMA)."""
     from oracle.oracle import Oracle, OracleEnv
     H = 4
     env = g1.G1Env(N, 10, 8, seed=7)
-    env.set_policy((256, 256), act)
+    env.set_policy((256, 256), act, precision="fp32-ffma" if path == "fp32-ffma" else "fp32")
     env.reset()
     oenv = OracleEnv(Oracle("f32"), N, 10, 8, seed=7)
     st = env.get_state()
@@ -160,7 +194,7 @@ def test_rollout_vs_oracle(g1, N, act):
     mean = torch.tensor(rng.normal(0, 0.1, 100), dtype=torch.float32).cuda()
     var = torch.tensor(rng.uniform(0.5, 2.0, 100), dtype=torch.float32).cuda()
     b = _bufs(H, N)
-    env.rollout(H, W, mean, var, *b.values())
+    (env.rollout_noalloc if path == "noalloc" else env.rollout)(H, W, mean, var, *b.values())
     torch.cuda.synchronize()
     ro = oenv.rollout(H, W.cpu().numpy(), mean.cpu().numpy(), var.cpu().numpy(), act=act)
     tol = dict(O=1e-3, A=1e-4, LP=1e-4, V=1e-4, R=1e-4, Vlast=1e-4)

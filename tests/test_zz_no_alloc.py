@@ -61,3 +61,48 @@ def test_noalloc_rejects_policy_beyond_static_area():
         env.rollout_noalloc(H, W, torch.zeros(100, device="cuda"), torch.ones(100, device="cuda"), *b)
     lib.g1_env_clear_error()
     env.close()
+
+
+def test_noalloc_rejects_bf16_policy_and_value_net():
+    """The static area only backs the fp32 in-kernel policy: an env set to the bf16
+    tensor-core policy, or given a separate value network, is rejected with an error rather
+    than run with a mismatched weight layout."""
+    import g1env
+    lib = g1env.load_library()
+    N, H = 16, 1
+    env = g1env.G1Env(N, 10, 8, seed=2)
+    env.reset()
+    mean, var = torch.zeros(100, device="cuda"), torch.ones(100, device="cuda")
+    env.set_policy((512,), "elu", precision="bf16")
+    W = g1env.pack_weights(g1env.init_policy_normal(g1env.AC(100, 29, (512,), "elu").cuda(), seed=0)).detach()
+    with pytest.raises(g1env.G1Error, match="fp32 in-kernel policy"):
+        env.rollout_noalloc(H, W, mean, var, *_bufs(H, N))
+    lib.g1_env_clear_error()
+    env.set_policy((256, 256), "elu", precision="bf16")
+    env.set_value_net((64,))
+    with pytest.raises(g1env.G1Error, match="fp32 in-kernel policy"):
+        env.rollout_noalloc(H, W, mean, var, *_bufs(H, N))
+    lib.g1_env_clear_error()
+    env.close()
+
+
+def test_noalloc_leaves_free_device_memory_unchanged():
+    """After a first call (which looks up the area's address), further calls change the
+    device's free memory by nothing: no allocation by the library or the CUDA runtime."""
+    import g1env
+    g1env.load_library()
+    N, H = 64, 2
+    env = g1env.G1Env(N, 10, 8, seed=5)
+    env.reset()
+    W = g1env.pack_weights(g1env.init_policy_normal(g1env.AC(100, 29).cuda(), seed=3)).detach()
+    mean, var = torch.zeros(100, device="cuda"), torch.ones(100, device="cuda")
+    b = _bufs(H, N)
+    env.rollout_noalloc(H, W, mean, var, *b)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        env.rollout_noalloc(H, W, mean, var, *b)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert np.isfinite(b[0].cpu().numpy()).all()
+    env.close()

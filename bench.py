@@ -31,6 +31,13 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "g1.cu_b200"))
 
 N_PER_GPU, H, S, PGS = 8192, 32, 10, 8
+OBS, ACT = 100, 29
+# DRAM traffic of one config-2 k_g1 launch (H = 32), dram__bytes_read.sum + dram__bytes_write.sum
+# from one ncu capture of the full-size launch (profiles/k_g1_rollout_n8192_h32.md)
+TRAFFIC_PER_LAUNCH = 6.55e6 + 91.92e6
+TRAFFIC_SOURCE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum (1 pass) of one full-size H=32 k_g1 "
+                  "launch: 6.55 MB read + 91.92 MB written; below the algorithmic bytes because ~48 MB of "
+                  "trajectory stores are still dirty in the 126 MB L2 when the kernel ends")
 METRIC = "fused-rollout substeps/s per box at 1/2/4/8 B200 (N=8192/GPU, H=32); % roofline"
 CONFIG = {"workload": "config2: fused PPO rollout, N=8192 worlds/GPU, H=32, S=10, PGS 8, "
                       "policy 100-256-256(ELU)-29+value fp32 random-init",
@@ -129,6 +136,18 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def all_ranks(x, world):
+    """x of every rank (rank order)."""
+    if world == 1:
+        return [x]
+    import torch
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    out = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(world)]
+    dist.all_gather(out, torch.tensor([x], dtype=torch.float64, device=dev))
+    return [float(t.item()) for t in out]
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -166,23 +185,45 @@ def cpu_baseline(steps_sample=None, worlds_sample=None, target_s=10.0):
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the CPU implementation of the path (the oracle port, bit-identical
+    to the reference's fp32 physics; the reference has no CPU rollout of its own besides
+    MuJoCo, which is not installed) on all host threads.  Each timed step is the FULL
+    config-2 workload -- one rollout of N_PER_GPU worlds x H control steps x S substeps,
+    continuing from the previous step's state, as the GPU arm does -- timed by wall clock
+    (one process, no GPU).  Warm-up steps are one control step each (thread-pool start)."""
     if rank != 0:
         return
-    t_all = []
+    import torch  # noqa: F401  (policy init uses torch)
+    import g1env
+    from oracle.oracle import Oracle, OracleEnv
+    cores = os.cpu_count() or 1
+    env = OracleEnv(Oracle("f32"), N_PER_GPU, S, PGS, seed=1)
+    env.reset()
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (256, 256), "elu"), seed=0)
+    W = g1env.pack_weights(ac).detach().numpy()
+    mean, var = np.zeros(100, np.float32), np.ones(100, np.float32)
     for _ in range(args.warmup):
-        cpu_baseline(1, 64)
-    cal = cpu_baseline(2, 1024)
-    steps = int(np.clip(12.0 * cal["value"] / (2048 * S * max(args.steps, 1)), 1, 512))
-    for _ in range(args.steps):   # each step: a bounded sample of ~12/K s of CPU work
-        cb = cpu_baseline(steps, 2048)
-        t_all.append(cb["value"])
-    v = float(np.mean(t_all))
-    ms = 1e3 * N_PER_GPU * H * S / v
+        env.rollout(1, W, mean, var, act="elu")
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        env.rollout(H, W, mean, var, act="elu")
+        ts.append(time.perf_counter() - t0)
+    env.close()
+    ms = 1e3 * float(np.mean(ts))
+    v = N_PER_GPU * H * S / (ms * 1e-3)  # the host's rate: its cores are the same at any N
+    cb = {"value": v, "unit": "substeps/s", "cores": cores, "kind": "port",
+          "sample": f"the full config-2 workload per step: {N_PER_GPU} worlds x {H} control steps x {S} substeps "
+                    f"with the ELU policy, CPU oracle fp32 (bit-identical to the reference's fp32 physics), "
+                    f"OpenMP {cores} threads; {args.steps} steps, mean {ms:.0f} ms"}
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "substeps/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": CONFIG, "cpu_baseline": dict(cb, value=v),
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (env-generated states, random-init policy)",
+            "config": dict(CONFIG, parallelism=f"world shards x{world}, no rollout communication"),
+            "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "substeps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if world > 1:
+        line["note"] = "rank 0 alone ran (one host, the same cores at any N): value is the host's rate on one rank's share"
     print(json.dumps(line), flush=True)
 
 
@@ -395,6 +436,7 @@ def main():
     ck = clocks.stop(t_start, t_end)
     ms_local = sum(a.elapsed_time(b) for a, b in times) / args.steps
     ms = max_over_ranks(ms_local, world)
+    per_rank_ms = all_ranks(ms_local, world)
     substeps = N * H * S
     value = world * substeps / (ms * 1e-3)
 
@@ -422,12 +464,20 @@ def main():
 
     # --- roofline of the dominant kernel (k_g1): algorithmic FP32 FLOPs / kernel time
     flop_sub = float((hist * flops_per_ncon()).sum() / max(hist.sum(), 1))
-    flops_launch = substeps * flop_sub + N * (H + 1) * MLP_FLOP_PER_WORLD_STEP
+    phys_flops = substeps * flop_sub
+    mlp_flops = N * (H + 1) * MLP_FLOP_PER_WORLD_STEP
+    flops_launch = phys_flops + mlp_flops
     peaks, peak_src = load_peaks()
     sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
     clk = ck.get("sm_max_mhz") or peaks.get("sm_max_mhz", 1965.0)
     fp32_peak = sm_count * 128 * 2 * clk * 1e6 / 1e12  # nominal FP32 FMA peak at max SM clock
     achieved = flops_launch / (ms * 1e-3) / 1e12
+    phys_achieved = phys_flops / (ms * 1e-3) / 1e12
+    mlp_achieved = mlp_flops / (ms * 1e-3) / 1e12
+    bf16_peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1590.0)))
+    # algorithmic HBM bytes of one launch: trajectory O/A/LP/V/R/D written once (133 floats per
+    # world-step), Vlast, the state read and written once, the packed weights and obs stats read
+    algo_bytes = 4 * (N * H * (OBS + ACT + 4) + N + 2 * N * (36 + 35 + 29 + 1) + W.numel() + 200)
     ref_ms = None
     if rank == 0 and not args.no_ref_kernel:
         try:
@@ -448,17 +498,29 @@ def main():
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (env-generated states, random-init policy)",
                 "config": dict(CONFIG, parallelism=f"world shards x{world}, no rollout communication"),
                 "e2e": {"value": world * substeps / (ems * 1e-3), "unit": "substeps/s", "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h},
+                        "d2h_bytes_per_step": d2h,
+                        "note": "policy weights and obs stats copied in, rewards / dones / bootstrap values copied "
+                                "out every step; the trajectory stays on the device, where the trainer reads it "
+                                "in place (ppo_fused.py)"},
                 "gpu_launches": 2 * args.steps,
-                "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
-                             "frac": achieved / fp32_peak, "traffic": 72.5e6,
-                             "traffic_source": "ncu dram__bytes_read+write of one H=2 launch (4.53 MB), scaled x16 to H=32 (profiles/k_g1_rollout_n8192_h32.md)",
-                             "peak_source": f"nominal FP32 FMA rate: {sm_count} SMs x 128 lanes x 2 x {clk:.0f} MHz; the policy "
-                                            f"MLP (counted at its algorithmic fp32 FLOPs) runs on the tensor cores "
-                                            f"(MEASURED_PEAKS.json has no FP32 figure; its hbm/bf16 peaks are {peak_src})",
+                "roofline": {"bound": "fp32", "achieved": phys_achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+                             "frac": phys_achieved / fp32_peak,
+                             "what": "k_g1 physics: algorithmic FP32 FLOPs of the substeps (FK + env_qacc by contact "
+                                     "count) / k_g1 launch time (CUDA events) vs the nominal FP32 rate",
+                             "traffic": TRAFFIC_PER_LAUNCH, "algorithmic_bytes": algo_bytes,
+                             "traffic_source": TRAFFIC_SOURCE,
+                             "peak_source": f"nominal FP32 FMA rate: {sm_count} SMs x 128 lanes x 2 x {clk:.0f} MHz "
+                                            f"(MEASURED_PEAKS.json has no FP32 figure)",
                              "flop_per_substep": flop_sub, "ncon_hist": hist.tolist(),
-                             "ncon_hist_source": "the 2 untimed rollouts just before the timed ones"},
+                             "ncon_hist_source": "the 2 untimed rollouts just before the timed ones",
+                             "policy_mlp": {"bound": "tensor", "achieved": mlp_achieved, "peak": bf16_peak,
+                                            "unit": "TFLOP/s", "frac": mlp_achieved / bf16_peak,
+                                            "what": "config-2 MLP FLOPs (fp32 semantics, run as split-bf16 tcgen05 "
+                                                    "MMAs inside k_g1) over the whole k_g1 launch time, vs "
+                                                    f"MEASURED_PEAKS.json bf16_tflops_sustained ({peak_src})"},
+                             "all_flops": {"achieved": achieved, "frac_of_fp32": achieved / fp32_peak}},
                 "clocks": ck,
+                "per_rank_ms": per_rank_ms,
                 "reference_kernel": None if ref_ms is None else {
                     "ms_per_step": ref_ms, "value": substeps / (ref_ms * 1e-3), "unit": "substeps/s",
                     "what": "reference k_rollout (src/g1_env.cu) built for sm_100a, same N/H/S, 1 GPU"}}

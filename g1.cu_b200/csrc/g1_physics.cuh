@@ -202,7 +202,7 @@ __device__ unsigned long long g_prof[64];
 #define PROF_RESTART()
 #define PROF_MARK(i) do { } while (0)
 #endif
-enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_CS_LOAD, P_CS_REWARD, P_CS_STORE, P_SORT, P_TOTAL, P_LS_BACK, P_LS_BASE, P_LS_FWD, P_TF_EPI1, P_TF_EPI2, P_NPHASE };
+enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_CS_LOAD, P_CS_REWARD, P_CS_STORE, P_SORT, P_TOTAL, P_LS_BACK, P_LS_BASE, P_LS_FWD, P_TF_EPI1, P_TF_EPI2, P_F1B, P_BASE_PULL, P_BASE_DM, P_NPHASE };
 
 // pyramid coefficients d_k = DC[k] of the 3-basis (env_qacc.cuh:98-100,154-155)
 __device__ __forceinline__ float dcoef(int k, int a) {
@@ -396,6 +396,7 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
             __syncwarp();
         }
     }
+    PROF_MARK(P_F1);
     // F1, second pass: the body forces and kept world inertias, one lane per (world, body),
     // from the kinematics the chain walk stashed (in place: a body's stash sits in its own
     // BQ / FOWN rows, its orientation in the idle contact workspace)
@@ -414,7 +415,7 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
         body_force_keep(T, b, quat, cpos, vw, vv, mk3(a01.x, a01.y, a23.x), mk3(a23.y, a45.x, a45.y), fo, bq);
     }
     __syncwarp();
-    PROF_MARK(P_F1);
+    PROF_MARK(P_F1B);
     // contact detection needs only F1's kept frames.  With contacts in the group (and
     // allow_defer), the base solve and F2 are left to the contact solve's back-solve step
     // (lane_solve, four more lanes), off the path to the contact batch.
@@ -552,6 +553,7 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
             }
     }
     __syncwarp();
+    PROF_MARK(P_BASE_PULL);
     float q6[6];
     if (w < GW) {
         // Dm[k*6+l] = S_k . U6_l (+ diag); lane cl: rows k = cl, cl+4
@@ -577,6 +579,7 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
         }
     }
     __syncwarp();
+    PROF_MARK(P_BASE_DM);
     if (w < GW && cl == 0) {
         // 6x6 Cholesky of Dm and the base solve in registers (aba_factor.cuh:103-107,
         // 148-152); one lane per world

@@ -526,56 +526,83 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     }
     PROF_MARK(P_B1);
 
-    // ---- floating base.  Lanes 4w..4w+3 of world w.
-    float* U6 = fr + WL::FU6;
-    float* L6 = fr + WL::FL6;
-    float base_ia[21], base_f[6], base_pa[6];
-    if (w < GW) {
-        // every lane of the world pulls the pelvis children (descending) into registers
-        body_ia_kept(T, 1, BQ + 9, base_ia);
+    // ---- floating base: 8 lanes per world, lanes 4w + c and 16 + 4w + c (c = 0..3) of
+    // world w, sub-lane k8 = c (+4).  Same arithmetic, entry by entry, as one lane doing it all
+    // (aba_factor.cuh:90-108, 128-155); only the lower triangle of Dm is formed (the Cholesky
+    // and the solves read nothing else).
+    const int wb = (lane & 15) >> 2, k8 = (lane & 3) + ((lane >> 4) << 2);
+    float* frb = grp + wb * WFLOATS;
+    const float* Sb = frb + WL::S;
+    float* U6 = frb + WL::FU6;
+    float* L6 = frb + WL::FL6;
+    float* BA = frb + WL::HF;  // pelvis IA [21], f [6], pA [6] (F1's hand-off area is dead now)
+    const float* bdtb = bdt_all;
+    float* biasb = nullptr;
+    if (!bdt_all && bdt_w) {
 #pragma unroll
-        for (int i = 0; i < 6; ++i) { base_f[i] = FOWN[6 + i]; base_pa[i] = 0.f; }
-        for (int q = T.child_start[1]; q < T.child_start[2]; ++q) {
-            const float* hb = fr + WL::HB + 36 * T.head_chain[T.child_list[q]];
+        for (int k = 0; k < GW; ++k) bdtb = (wb == k) ? bdt_w[k] : bdtb;
+    }
+    if (bias_out) {
 #pragma unroll
-            for (int i = 0; i < 21; ++i) base_ia[i] += hb[i];
+        for (int k = 0; k < GW; ++k) biasb = (wb == k) ? bias_out[k] : biasb;
+    }
+    static_assert(20 * G1_MAXBRANCH >= 33, "the pelvis accumulators fit in the F1 hand-off area");
+    // the pelvis's own IA / f, then its children's contributions in descending child index
+    {
+        // the pelvis's children (at most 4: the G1 has 3), their chain-head hand-offs in HB
+        const int q0 = T.child_start[1], nch = T.child_start[2] - q0;
+        int hoff[4];
 #pragma unroll
-            for (int i = 0; i < 6; ++i) { base_f[i] += hb[21 + i]; base_pa[i] += hb[27 + i]; }
-        }
-        // U6[i*6+l] = (IA S_l)[i]: lane cl computes columns l = cl, cl+4 (< 6)
-        for (int l = cl; l < 6; l += 4)
+        for (int c = 0; c < 4; ++c) hoff[c] = c < nch ? WL::HB + 36 * T.head_chain[T.child_list[q0 + c]] : 0;
+        float ia1[21];
+        body_ia_kept(T, 1, frb + WL::BQ + 9, ia1);
 #pragma unroll
-            for (int i = 0; i < 6; ++i) {
-                float acc = 0.f;
+        for (int m = 0; m < 5; ++m) {
+            const int e = k8 + 8 * m;
+            if (e < 33) {
+                float v = (e >= 21 && e < 27) ? frb[WL::FOWN + 6 + (e - 21)] : 0.f;
 #pragma unroll
-                for (int j = 0; j < 6; ++j) acc += base_ia[sym6(i, j)] * S[6 * l + j];
-                U6[i * 6 + l] = acc;
+                for (int j = 0; j < 8; ++j)
+                    if (8 * m + j < 21) v = (k8 == j) ? ia1[8 * m + j] : v;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (c < nch) v += frb[hoff[c] + e];
+                BA[e] = v;
             }
+        }
+    }
+    __syncwarp();
+    // U6[i*6+l] = (IA S_l)[i]: 36 entries over the 8 lanes
+    for (int e = k8; e < 36; e += 8) {
+        const int i = e / 6, l = e % 6;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 6; ++j) acc += BA[sym6(i, j)] * Sb[6 * l + j];
+        U6[i * 6 + l] = acc;
     }
     __syncwarp();
     PROF_MARK(P_BASE_PULL);
-    float q6[6];
-    if (w < GW) {
-        // Dm[k*6+l] = S_k . U6_l (+ diag); lane cl: rows k = cl, cl+4
-        for (int kk = cl; kk < 6; kk += 4)
+    // Dm[k*6+l] = S_k . U6_l (+ diag) for l <= k: 21 entries; u = (-bias + tau) - S^T pA: 6
+    for (int e = k8; e < 27; e += 8) {
+        if (e < 21) {
+            int k = 0;
 #pragma unroll
-            for (int l = 0; l < 6; ++l) {
-                float acc = 0.f;
+            for (int r = 1; r < 6; ++r) k += (e >= r * (r + 1) / 2) ? 1 : 0;
+            const int l = e - k * (k + 1) / 2;
+            float acc = 0.f;
 #pragma unroll
-                for (int i = 0; i < 6; ++i) acc += S[6 * kk + i] * U6[i * 6 + l];
-                L6[kk * 6 + l] = acc + (kk == l ? (T.armature[kk] + (bdt ? bdt[kk] : 0.f)) : 0.f);
-            }
-        // base bias and u = (-bias + tau) - S^T pA (all 6, every lane of the world)
-#pragma unroll
-        for (int kk = 0; kk < 6; ++kk) {
-            const float* sd = S + 6 * kk;
-            const float bd = sd[0] * base_f[0] + sd[1] * base_f[1] + sd[2] * base_f[2] + sd[3] * base_f[3] +
-                             sd[4] * base_f[4] + sd[5] * base_f[5];
-            if (bias && cl == 0) bias[kk] = bd;
+            for (int i = 0; i < 6; ++i) acc += Sb[6 * k + i] * U6[i * 6 + l];
+            L6[k * 6 + l] = acc + (k == l ? (T.armature[k] + (bdtb ? bdtb[k] : 0.f)) : 0.f);
+        } else {
+            const int kk = e - 21;
+            const float* sd = Sb + 6 * kk;
+            const float* bf = BA + 21;
+            const float bd = sd[0] * bf[0] + sd[1] * bf[1] + sd[2] * bf[2] + sd[3] * bf[3] + sd[4] * bf[4] + sd[5] * bf[5];
+            if (biasb) biasb[kk] = bd;
             float sp = 0.f;
 #pragma unroll
-            for (int i = 0; i < 6; ++i) sp += sd[i] * base_pa[i];
-            q6[kk] = (-bd + tau[kk]) - sp;
+            for (int i = 0; i < 6; ++i) sp += sd[i] * BA[27 + i];
+            frb[WL::QACC + kk] = (-bd + frb[WL::TAU + kk]) - sp;  // u of the base dofs, parked in qacc
         }
     }
     __syncwarp();
@@ -583,9 +610,13 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
     if (w < GW && cl == 0) {
         // 6x6 Cholesky of Dm and the base solve in registers (aba_factor.cuh:103-107,
         // 148-152); one lane per world
-        float Dm[36];
+        float Dm[36], q6[6];
 #pragma unroll
-        for (int k = 0; k < 36; ++k) Dm[k] = L6[k];
+        for (int i = 0; i < 6; ++i)
+#pragma unroll
+            for (int j = 0; j <= i; ++j) Dm[i * 6 + j] = L6[i * 6 + j];
+#pragma unroll
+        for (int k = 0; k < 6; ++k) q6[k] = qacc[k];
 #pragma unroll
         for (int i = 0; i < 6; ++i)
 #pragma unroll
@@ -596,11 +627,10 @@ __device__ int group_smooth(float* grp, const G1Tables& T, int lane, const float
                 if (i == j) Dm[i * 6 + i] = sqrtf(acc); else Dm[i * 6 + j] = acc / Dm[j * 6 + j];
             }
 #pragma unroll
-        for (int k = 0; k < 36; ++k) L6[k] = Dm[k];
-      if (defer) {  // the base solve and the root -> leaf pass run later, in lane_solve
+        for (int i = 0; i < 6; ++i)
 #pragma unroll
-        for (int k = 0; k < 6; ++k) qacc[k] = q6[k];
-      } else {
+            for (int j = 0; j <= i; ++j) L6[i * 6 + j] = Dm[i * 6 + j];
+      if (!defer) {  // else the base solve and the root -> leaf pass run later, in lane_solve
 #pragma unroll
         for (int i = 0; i < 6; ++i) {
             float acc = q6[i];

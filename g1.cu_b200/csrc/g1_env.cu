@@ -456,7 +456,9 @@ __device__ __forceinline__ void lockstep_barrier(const Params& P, int s) {
 __device__ __forceinline__ void idle_midbar(const Params& P) {
     if (P.lockstep > 0) {
         if (P.midbar & 1) substep_barrier();
+        PROF_BEGIN();
         if (P.midbar & 2) substep_barrier();
+        PROF_MARK(P_MIDBAR);
     }
 }
 

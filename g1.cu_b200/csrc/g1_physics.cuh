@@ -202,7 +202,7 @@ __device__ unsigned long long g_prof[64];
 #define PROF_RESTART()
 #define PROF_MARK(i) do { } while (0)
 #endif
-enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_CS_LOAD, P_CS_REWARD, P_CS_STORE, P_SORT, P_TOTAL, P_LS_BACK, P_LS_BASE, P_LS_FWD, P_TF_EPI1, P_TF_EPI2, P_F1B, P_BASE_PULL, P_BASE_DM, P_NPHASE };
+enum ProfPhase { P_POLICY = 0, P_F1, P_B1, P_BASE, P_F2, P_CSETUP, P_SOLVE, P_GRAM, P_PGS, P_DQ, P_STEP, P_WAIT, P_INTEG, P_DETECT, P_MLP, P_SAMPLE, P_MLP_L1, P_MLP_HEAD, P_BAR, P_ENERGY, P_TF_MMA, P_TF_EPI, P_CS_LOAD, P_CS_REWARD, P_CS_STORE, P_SORT, P_TOTAL, P_LS_BACK, P_LS_BASE, P_LS_FWD, P_TF_EPI1, P_TF_EPI2, P_F1B, P_BASE_PULL, P_BASE_DM, P_MIDBAR, P_NPHASE };
 
 // pyramid coefficients d_k = DC[k] of the 3-basis (env_qacc.cuh:98-100,154-155)
 __device__ __forceinline__ float dcoef(int k, int a) {
@@ -1224,7 +1224,12 @@ __device__ void group_qacc(float* grp, float* cw, const G1Tables& T, int lane, c
         }
     }
     if (B.nw > 0) solve(B);
+    PROF_BEGIN();
     if (midbar & 2) asm volatile("bar.sync 1, %0;" ::"r"(bar_threads) : "memory");
+#ifdef G1_PROF
+    (void)*(volatile const float*)grp;  // bar.sync blocks lazily: make the wait land here
+#endif
+    PROF_MARK(P_MIDBAR);
 }
 
 // ------------------------------------------------------------------ integration

@@ -139,6 +139,11 @@ class G1Env:
         _lib.g1_env_step(self.h, _p(act), _p(self._obs), _p(self._rew), _p(self._done)); _check()
         return self._obs.copy(), self._rew.copy(), self._done.copy()
 
+    def step_device(self, act, obs, rew, done):
+        """g1_env_step_device: one control step on CUDA tensors (act [N, 29] -> obs [N, 100],
+        rew [N], done [N]), asynchronous on the env's stream."""
+        _lib.g1_env_step_device(self.h, _dp(act), _dp(obs), _dp(rew), _dp(done)); _check()
+
     def set_stream(self, stream):
         _lib.g1_env_set_stream(self.h, ctypes.c_void_p(stream.cuda_stream if stream is not None else 0))
 
@@ -327,24 +332,37 @@ def runnorm_update_device(norm, obs_mom, rows_total):
     norm.count = norm.count + rows_total
 
 
-# ---------------- running obs normalizer (ppo.py:63-81) ----------------
+# ---------------- running obs normalizer (the state of ppo.py:63-81) ----------------
 class RunNorm:
-    """Running mean/var of observations (clipped normalisation)."""
+    """Running mean / variance of the raw observations and the clipped normalisation
+    z = clamp((o - mean) / sqrt(var + 1e-8), +-10) that the rollout kernel applies.
+
+    The state (mean, var, count) and its merge rule are the reference's (a batch of b rows
+    with moments (m_b, v_b) merged into (mean, var, count) by the parallel-variance formula).
+    Batches are reduced here in fp64 -- the same moments the device batch preparation
+    (g1_obs_prep + g1_runnorm_update) accumulates -- so a host update and a device update of
+    the same rows agree to fp32 rounding."""
 
     def __init__(self, dim, dev):
         self.mean = torch.zeros(dim, device=dev)
         self.var = torch.ones(dim, device=dev)
         self.count = 1e-4
 
-    def update_from_moments(self, bm, bv, b):
-        tot = self.count + b
-        delta = bm - self.mean
-        self.mean = self.mean + delta * b / tot
-        self.var = (self.var * self.count + bv * b + delta ** 2 * self.count * b / tot) / tot
+    def merge(self, m_b, v_b, b):
+        """Merge a batch of b rows with per-dimension mean m_b and (biased) variance v_b."""
+        n0, n = float(self.count), float(b)
+        tot = n0 + n
+        m0, v0 = self.mean.double(), self.var.double()
+        d = m_b.double() - m0
+        self.mean = (m0 + d * (n / tot)).float()
+        self.var = ((v0 * n0 + v_b.double() * n + d * d * (n0 * n / tot)) / tot).float()
         self.count = tot
 
-    def update(self, x):  # x: [B, dim]
-        self.update_from_moments(x.mean(0), x.var(0, unbiased=False), x.shape[0])
+    def update(self, x):
+        """Merge the rows of x [B, dim] (fp64 moments)."""
+        xd = x.detach().double()
+        m_b = xd.mean(0)
+        self.merge(m_b, (xd * xd).mean(0) - m_b * m_b, x.shape[0])
 
     def norm(self, x):
         return torch.clamp((x - self.mean) / torch.sqrt(self.var + 1e-8), -10.0, 10.0)
@@ -412,21 +430,29 @@ def init_policy_normal(ac, seed=0):
 
 @torch.no_grad()
 def evaluate(env, ac, norm, dev, steps=200):
-    """Deterministic (mean) policy roll through the host-loop step path (ppo.py:103-125)."""
-    obs = torch.tensor(env.reset(), device=dev)
-    N = env.N
-    dt_ctrl = 0.02
-    fwd = np.zeros(N); alive_len = np.zeros(N); done_any = np.zeros(N, bool)
-    vx_acc = np.zeros(N)
+    """Deterministic (mean-action) evaluation on the device-resident host-loop step path
+    (g1_env_step_device), reporting the metrics of the reference trainer's evaluate
+    (ppo.py:103-125): distance walked (base forward velocity, obs[:, 0], integrated over
+    the 0.02 s control step) until the first episode end, its mean and max over worlds, the
+    mean number of live steps, the fraction of worlds that ended an episode, and the mean
+    forward velocity while live.  Everything stays on the GPU; one host sync at the end."""
+    N, ctrl_dt = env.N, 0.02
+    obs = torch.as_tensor(env.reset(), device=dev)
+    rew = torch.zeros(N, device=dev)
+    done = torch.zeros(N, device=dev)
+    live = torch.ones(N, device=dev)
+    dist = torch.zeros(N, device=dev)
+    vsum = torch.zeros(N, device=dev)
+    nlive = torch.zeros(N, device=dev)
     for _ in range(steps):
-        mu, _, _ = ac(norm.norm(obs))
-        no, rw, dn = env.step(mu.cpu().numpy())
-        vx = no[:, 0]
-        live = ~done_any
-        fwd[live] += vx[live] * dt_ctrl
-        vx_acc[live] += vx[live]
-        alive_len[live] += 1
-        done_any |= dn.astype(bool)
-        obs = torch.tensor(no, device=dev)
-    return dict(fwd_mean=float(fwd.mean()), fwd_max=float(fwd.max()), ep_len_mean=float(alive_len.mean()),
-                fall_rate=float(done_any.mean()), vx_mean=float((vx_acc / np.maximum(alive_len, 1)).mean()))
+        mu = ac(norm.norm(obs))[0].contiguous()
+        env.step_device(mu, obs, rew, done)
+        vx = obs[:, 0]
+        dist += live * vx * ctrl_dt
+        vsum += live * vx
+        nlive += live
+        live = live * (done == 0).float()
+    fallen = 1.0 - live
+    out = torch.stack([dist.mean(), dist.max(), nlive.mean(), fallen.mean(),
+                       (vsum / nlive.clamp_min(1.0)).mean()]).tolist()
+    return dict(zip(("fwd_mean", "fwd_max", "ep_len_mean", "fall_rate", "vx_mean"), out))

@@ -89,25 +89,37 @@ def broadcast_params(module):
         dist.broadcast(p.data, 0)
 
 
+HALF_LOG_2PI = 0.9189385332046727
+
+
+def ppo_loss(ac, obs, act, old_logp, adv, ret, clip=0.2, vf_coef=0.5, ent_coef=0.01):
+    """The clipped-surrogate PPO objective the reference trainer minimises
+    (ppo_fused.py:121-140): policy term -E[min(r A, clip(r, 1 +- eps) A)], value term
+    vf_coef E[(V - R)^2], entropy bonus ent_coef E[H].  The diagonal Gaussian's log-density
+    and entropy are written in closed form from the mean and log-std:
+        log p(a) = sum_i [-(a_i - mu_i)^2 / (2 s_i^2) - log s_i - log sqrt(2 pi)],
+        H = sum_i [log s_i + 1/2 + log sqrt(2 pi)]."""
+    mu, std, val = ac(obs)
+    log_std = torch.log(std).expand_as(mu)
+    z = (act - mu) / std
+    logp = (-0.5 * z * z - log_std - HALF_LOG_2PI).sum(-1)
+    ratio = torch.exp(logp - old_logp)
+    surrogate = torch.minimum(ratio * adv, ratio.clamp(1.0 - clip, 1.0 + clip) * adv)
+    entropy = (log_std + 0.5 + HALF_LOG_2PI).sum(-1)
+    return -surrogate.mean() + vf_coef * (val - ret).square().mean() - ent_coef * entropy.mean()
+
+
 def ppo_update(ac, opt, b_o, b_a, b_lp, b_adv, b_ret, epochs=5, mb=4, clip=0.2):
-    """The clipped PPO update of ppo_fused.py:121-140 (+ gradient all-reduce)."""
+    """Epochs x minibatches of ppo_loss over a shuffled batch, with the gradients averaged
+    over ranks before clipping (max norm 0.5) and the optimiser step."""
     n = b_o.shape[0]
-    last = 0.0
+    size = n // mb
     params = list(ac.parameters())
+    last = 0.0
     for _ in range(epochs):
-        idx = torch.randperm(n, device=b_o.device)
-        for s in range(0, n, n // mb):
-            j = idx[s:s + n // mb]
-            mu, std, val = ac(b_o[j])
-            dist = torch.distributions.Normal(mu, std)
-            lp = dist.log_prob(b_a[j]).sum(-1)
-            ratio = (lp - b_lp[j]).exp()
-            s1 = ratio * b_adv[j]
-            s2 = torch.clamp(ratio, 1 - clip, 1 + clip) * b_adv[j]
-            pl = -torch.min(s1, s2).mean()
-            vl = (val - b_ret[j]).pow(2).mean()
-            ent = dist.entropy().sum(-1).mean()
-            loss = pl + 0.5 * vl - 0.01 * ent
+        perm = torch.randperm(n, device=b_o.device)
+        for j in perm[: size * mb].view(mb, size).unbind(0):
+            loss = ppo_loss(ac, b_o[j], b_a[j], b_lp[j], b_adv[j], b_ret[j], clip)
             opt.zero_grad()
             loss.backward()
             allreduce_grads(params)

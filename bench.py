@@ -303,6 +303,61 @@ def profile_case3(h):
     print("profile case 3 done")
 
 
+PHASES = ["policy", "F1", "B1", "base", "F2", "contact_setup", "back_solves", "gram", "pgs", "dq", "pd_torque",
+          "end_of_step_wait", "integrate", "detect", "mlp_layer0", "sampling", "mlp_layer1", "mlp_head",
+          "substep_barrier_wait", "energy", "mlp_mma_wait", "mlp_epilogue", "step_state_load", "reward_done",
+          "state_store_reset", "contact_sort", "kernel_total", "solve_leaf_to_root", "solve_base",
+          "solve_root_to_leaf", "mlp_epilogue_stage", "mlp_epilogue_act", "F1_pass2", "base_pull_U6",
+          "base_Dm_q6", "midbar_wait"]
+# sub-phases: counted inside another phase, left out of the unattributed remainder
+SUBPHASES = {"mlp_layer0", "mlp_layer1", "mlp_head", "sampling", "mlp_mma_wait", "mlp_epilogue",
+             "mlp_epilogue_stage", "mlp_epilogue_act", "solve_leaf_to_root", "solve_base", "solve_root_to_leaf"}
+
+
+def phase_profile(h):
+    """Per-phase cycle attribution of k_g1 (attribution only, not a benchmark): builds the
+    -DG1_PROF variant of the library (clock64 counters around each phase, summed per warp)
+    into _build/libg1env_prof.so, runs one warm-up and one measured config-2 rollout of
+    horizon h, and prints the mean cycles per warp per control step of each phase."""
+    import ctypes
+    import torch
+    import g1env
+    from build import ARCH, CSRC, FLAGS
+    out_dir = os.path.join(ROOT, "_build")
+    os.makedirs(out_dir, exist_ok=True)
+    lib_path = os.path.join(out_dir, "libg1env_prof.so")
+    r = subprocess.run(["nvcc"] + ARCH + FLAGS + ["-DG1_PROF", os.path.join(CSRC, "g1_env.cu"), "-o", lib_path],
+                       capture_output=True, text=True)
+    if r.returncode:
+        raise RuntimeError(r.stderr)
+    g1env.load_library(lib_path)
+    lib = g1env._lib
+    lib.g1_prof_read.argtypes = [ctypes.c_void_p]
+    N = N_PER_GPU
+    env = g1env.G1Env(N, S, PGS, seed=1)
+    env.set_policy((256, 256), "elu")
+    env.reset()
+    ac = g1env.init_policy_normal(g1env.AC(100, 29, (256, 256), "elu").cuda(), seed=0)
+    W = g1env.pack_weights(ac).detach()
+    mean, var = torch.zeros(100, device="cuda"), torch.ones(100, device="cuda")
+    z = lambda *sh: torch.zeros(*sh, device="cuda")
+    bufs = [z(h, N, 100), z(h, N, 29), z(h, N), z(h, N), z(h, N), z(h, N), z(N)]
+    env.rollout(h, W, mean, var, *bufs)
+    cnt = (ctypes.c_ulonglong * 64)()
+    lib.g1_prof_read(cnt)  # clears the counters
+    env.rollout(h, W, mean, var, *bufs)
+    lib.g1_prof_read(cnt)
+    sm = torch.cuda.get_device_properties(0).multi_processor_count
+    wb = (N + sm - 1) // sm
+    nwarps = ((N + wb - 1) // wb) * 7
+    per = {n: round(cnt[i] / nwarps / h) for i, n in enumerate(PHASES)}
+    per["unattributed"] = per["kernel_total"] - sum(v for k, v in per.items() if k != "kernel_total" and k not in SUBPHASES)
+    batches = [round(cnt[47 + c] / h / (nwarps // 7), 2) for c in range(1, 9)]
+    print(json.dumps({"N": N, "H": h, "cycles_per_warp_per_control_step": per,
+                      "contact_batches_per_cta_per_control_step_by_size_1_to_8": batches}))
+    env.close()
+
+
 def other_configs(dev):
     """Informational timings of BASELINE configs 1 and 3 on this GPU (CUDA events, L2 flushed
     between timed calls); the headline metric is config 2."""
@@ -378,7 +433,12 @@ def main():
                     help="run two H-step rollouts of the config-2 worlds and exit (small case for ncu captures)")
     ap.add_argument("--profile-case3", type=int, default=0, metavar="H",
                     help="run two H-step rollouts of the config-3 workload and exit (small case for ncu captures)")
+    ap.add_argument("--phase-profile", type=int, default=0, metavar="H",
+                    help="per-phase cycle attribution of k_g1 from a -DG1_PROF build (horizon H) and exit")
     args = ap.parse_args()
+    if args.phase_profile:
+        phase_profile(args.phase_profile)
+        return
     if args.profile_case3:
         profile_case3(args.profile_case3)
         return

@@ -16,8 +16,8 @@ restatement of the reward and observation (oracle/g1_oracle.c) to the reference 
 Tolerances: the first step's observation within relative L2 1e-5 per world (one control
 step of the same fp32 arithmetic, differently rounded); later observations within 1e-3
 absolute (rounding differences grow over contact-rich substeps, as in the rollout gates);
-reward within 1e-4; done flags exact.  Rollouts run H = 4 control steps, as the rollout
-gates against the oracle."""
+reward within 1e-4; done flags exact.  Rollouts run H = 4 control steps at N = 128, as the
+rollout gates against the oracle, and H = 2 at the full N = 8192."""
 import ctypes
 import os
 
@@ -107,10 +107,10 @@ def test_host_step_obs_reward_done_vs_reference_env(ref, g1):
     oenv.close()
 
 
-@pytest.mark.parametrize("precision", ["fp32", "fp32-ffma"])
-def test_fused_rollout_vs_reference_env(ref, g1, precision):
+@pytest.mark.parametrize("precision,N,H", [("fp32", 128, 4), ("fp32-ffma", 128, 4), ("fp32", 8192, 2)])
+def test_fused_rollout_vs_reference_env(ref, g1, precision, N, H):
+    """N = 8192 runs the production grid (147 CTAs, two rounds of groups per CTA)."""
     from oracle.oracle import Oracle, OracleEnv
-    N, H = 128, 4
     h, qp, _ = _ref_reset(ref, N, seed=23)
     zv, zp, zs = np.zeros((N, NV), np.float32), np.zeros((N, ACT), np.float32), np.zeros(N, np.int32)
     env = g1.G1Env(N, 10, 8, seed=23)

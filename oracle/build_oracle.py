@@ -5,7 +5,8 @@ Outputs (all git-ignored, all travel with the repository snapshot to a GPU box):
   oracle/liboracle_f32.so, oracle/liboracle_f64.so   -- this repository's C restatement
   oracle/_ref/libg1ref_host_f32.so / _f64.so / _f32_mu1.so
                                                      -- reference physics headers, host C++
-  oracle/_ref/libg1ref_cuda.so                       -- reference physics, CUDA sm_100a harness
+  oracle/_ref/libg1ref_cuda.so, _mu1.so              -- reference physics, CUDA sm_100a harness
+                                                        (model friction 0.6, and 1.0)
   oracle/_ref/libg1env_ref.so                        -- the reference's g1_env.cu as shipped,
                                                         compiled for sm_100a (its own C-ABI)
   oracle/_ref/trainer/scripts/ppo.py, ppo_fused.py   -- the reference's trainer, staged
@@ -63,9 +64,11 @@ def build_ref(ref_root=None, force=False, cuda=True):
             _run(["g++", "-O2", "-shared", "-fPIC", "-ffp-contract=off", "-w", "-I", src_dir] + flags + [shim, "-o", out])
     if cuda:
         harness = os.path.join(HERE, "ref_cuda_harness.cu")
-        out = os.path.join(out_dir, "libg1ref_cuda.so")
-        if force or _stale(out, [harness] + ref_srcs):
-            _run(["nvcc"] + ARCH + ["-O3", "-Xcompiler", "-fPIC", "--shared", "-w", "-I", src_dir, harness, "-o", out])
+        for tag, flags in (("", []), ("_mu1", ["-DREF_MU=1.0f"])):
+            out = os.path.join(out_dir, f"libg1ref_cuda{tag}.so")
+            if force or _stale(out, [harness] + ref_srcs):
+                _run(["nvcc"] + ARCH + ["-O3", "-Xcompiler", "-fPIC", "--shared", "-w", "-I", src_dir] + flags +
+                     [harness, "-o", out])
         out = os.path.join(out_dir, "libg1env_ref.so")
         env_src = os.path.join(src_dir, "g1_env.cu")
         if force or _stale(out, [env_src] + ref_srcs):

@@ -7,6 +7,13 @@
 // reference tree is present; never shipped.
 #include <cstdio>
 #include <cuda_runtime.h>
+// -DREF_MU=x overrides the model friction G1_FOOT_MU (the reference hard-codes 0.6); the
+// model header is included first so the override holds in every physics header after it
+#include "g1_model.h"
+#ifdef REF_MU
+#undef G1_FOOT_MU
+#define G1_FOOT_MU REF_MU
+#endif
 #include "dynamics.cuh"
 #include "aba.cuh"
 #include "aba_factor.cuh"

@@ -25,6 +25,7 @@ pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_CUDA = os.path.join(ROOT, "oracle", "_ref", "libg1ref_cuda.so")
+REF_CUDA_MU1 = os.path.join(ROOT, "oracle", "_ref", "libg1ref_cuda_mu1.so")  # friction 1.0 (config 1)
 
 
 def relrows(a, b):
@@ -70,6 +71,24 @@ def test_qacc_vs_reference_cuda_fp32(gpu_qacc, states):
     assert L.ref_cuda_qacc(n, *[vp(t) for t in dq], 8, vp(out)) == 0
     e = relrows(gpu_qacc["qacc"], out.cpu().numpy())
     print(f"qacc vs reference CUDA fp32 over {n} states: max {e.max():.2e}, p99 {np.percentile(e, 99):.2e}")
+    assert e.max() <= 1e-5, e.max()
+    assert np.percentile(e, 99) <= 5e-6
+
+
+@pytest.mark.skipif(not os.path.exists(REF_CUDA_MU1), reason="reference CUDA build not present")
+def test_qacc_vs_reference_cuda_fp32_mu1(g1, states):
+    """The per-substep qacc gate at friction 1.0 against the reference's
+    CUDA physics compiled with its friction constant overridden to 1.0."""
+    qp, qv, bdt = states
+    n = qp.shape[0]
+    L = ctypes.CDLL(REF_CUDA_MU1)
+    dq = [torch.tensor(x).cuda().contiguous() for x in (qp, qv, np.zeros((n, 35), np.float32), np.tile(bdt, (n, 1)))]
+    out = torch.zeros(n, 35, device="cuda")
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    assert L.ref_cuda_qacc(n, *[vp(t) for t in dq], 8, vp(out)) == 0
+    got = g1.qacc_batch(dq[0], dq[1], None, torch.tensor(bdt).cuda(), 8, 1.0)["qacc"].cpu().numpy()
+    e = relrows(got, out.cpu().numpy())
+    print(f"qacc (mu 1.0) vs reference CUDA fp32 over {n} states: max {e.max():.2e}, p99 {np.percentile(e, 99):.2e}")
     assert e.max() <= 1e-5, e.max()
     assert np.percentile(e, 99) <= 5e-6
 

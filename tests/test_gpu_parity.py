@@ -93,8 +93,8 @@ def test_qacc_vs_reference_cuda_fp32_mu1(g1, states):
     assert np.percentile(e, 99) <= 5e-6
 
 
-@pytest.mark.skipif(not os.path.exists(REF_CUDA), reason="reference CUDA build not present")
-def test_substep_qpos_qvel_vs_reference_cuda_fp32(g1, states):
+@pytest.mark.parametrize("lib,mu", [(REF_CUDA, 0.6), (REF_CUDA_MU1, 1.0)])
+def test_substep_qpos_qvel_vs_reference_cuda_fp32(g1, states, lib, mu):
     """One full substep -- PD torque, env_qacc, velocity update and guard, integrate_pos
     (src/g1_env.cu:123-161, dynamics.cuh:333-355) -- against the reference's own CUDA fp32
     code on the same 4096 states and random actions: per-state relative L2 error of qpos and
@@ -104,12 +104,14 @@ def test_substep_qpos_qvel_vs_reference_cuda_fp32(g1, states):
     n = qp.shape[0]
     rng = np.random.default_rng(17)
     act = rng.uniform(-1, 1, (n, 29)).astype(np.float32)
-    L = ctypes.CDLL(REF_CUDA)
+    if not os.path.exists(lib):
+        pytest.skip("reference CUDA build not present")
+    L = ctypes.CDLL(lib)
     vp = lambda t: ctypes.c_void_p(t.data_ptr())
     d = [torch.tensor(x).cuda().contiguous() for x in (qp, qv, act)]
     qp_ref, qv_ref = torch.zeros(n, 36, device="cuda"), torch.zeros(n, 35, device="cuda")
     assert L.ref_cuda_substep(n, *[vp(t) for t in d], 8, vp(qp_ref), vp(qv_ref)) == 0
-    env = g1.G1Env(n, 1, 8, seed=3)
+    env = g1.G1Env(n, 1, 8, seed=3, mu=mu)
     env.set_state(qp, qv, np.zeros((n, 29), np.float32), np.zeros(n, np.int32))
     _, _, done = env.step(act)
     gq, gv = env.get_state()[:2]
@@ -118,7 +120,7 @@ def test_substep_qpos_qvel_vs_reference_cuda_fp32(g1, states):
     assert keep.sum() >= 0.95 * n
     eq = relrows(gq[keep], qp_ref.cpu().numpy()[keep])
     ev = relrows(gv[keep], qv_ref.cpu().numpy()[keep])
-    print(f"one substep vs reference CUDA fp32 over {keep.sum()} states: qpos max {eq.max():.2e}, "
+    print(f"one substep (mu {mu}) vs reference CUDA fp32 over {keep.sum()} states: qpos max {eq.max():.2e}, "
           f"qvel max {ev.max():.2e} p99 {np.percentile(ev, 99):.2e}")
     assert eq.max() <= 1e-5, eq.max()
     assert ev.max() <= 1e-5, ev.max()

@@ -24,6 +24,14 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+// Each CTA walks a tile's K chunks starting at chunk blockIdx.x (mod the chunk count): the
+// CTAs working on tiles of one weight block then read different chunks of it at any moment
+// instead of all 148 reading the same 16 KB from the same L2 slices.  The fp32 accumulation
+// order depends only on the CTA index, so results stay deterministic for a given grid.
+#ifndef G1_GEMM_KROT
+#define G1_GEMM_KROT 1
+#endif
+
 namespace g1gemm {
 
 constexpr int BM = 128, BK = 64, STAGES = 4;
@@ -124,8 +132,13 @@ k_gemm(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensor
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s32(&S.full[stage])),
                              "r"((BM + BN) * BK * 2)
                              : "memory");
-                tma_load_2d(S.a[stage], &tmx, kb * BK, m0, &S.full[stage]);
-                tma_load_2d(S.b[stage], &tmw, kb * BK, n0, &S.full[stage]);
+#if G1_GEMM_KROT
+                const int kc = (kb + (int)blockIdx.x) % nk;
+#else
+                const int kc = kb;
+#endif
+                tma_load_2d(S.a[stage], &tmx, kc * BK, m0, &S.full[stage]);
+                tma_load_2d(S.b[stage], &tmw, kc * BK, n0, &S.full[stage]);
                 if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
         }

@@ -1,7 +1,7 @@
 """PPO on the fused GPU rollout, one process per GPU (the reference's scripts/ppo_fused.py
 training loop, ppo_fused.py:47-171, with world sharding across ranks).
 
-    python g1.cu_b200/ppo_fused.py [iters] [n_worlds_per_gpu] [--smoke] [--tag=name] [--config4] [--no-eval]
+    python g1.cu_b200/ppo_fused.py [iters] [n_worlds_per_gpu] [--smoke] [--tag=name] [--config4] [--no-eval] [--tf32]
     torchrun --nproc-per-node 8 g1.cu_b200/ppo_fused.py 1500 8192
     torchrun --nproc-per-node 8 g1.cu_b200/ppo_fused.py 3 65536 --config4 --no-eval
 
@@ -145,6 +145,11 @@ def main():
     H = 16 if smoke else 32
     config4 = "--config4" in sys.argv
     do_eval = "--no-eval" not in sys.argv
+    if "--tf32" in sys.argv:
+        # opt-in: the update's matmuls on the tensor cores in TF32 (10-bit mantissa products,
+        # fp32 accumulation); off by default, so the update's arithmetic is the reference's fp32
+        torch.backends.cuda.matmul.allow_tf32 = True
+        torch.backends.cudnn.allow_tf32 = True
     tag = next((a.split("=", 1)[1] for a in sys.argv if a.startswith("--tag=")), "fused")
     out_dir = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "runs")
     os.makedirs(out_dir, exist_ok=True)
